@@ -1,0 +1,129 @@
+/*
+ * scalesweep_b200 -- C ABI of the B200 (sm_100a) scale-sweep NVFP4 quantizer.
+ *
+ * Plain pointers and sizes only.  Every data pointer is a CUDA device pointer
+ * of the current device unless stated otherwise; `stream` is a cudaStream_t
+ * passed as void* (NULL = legacy default stream).  All entry points are
+ * asynchronous with respect to the host, enqueue on `stream`, never allocate,
+ * never synchronise, and return an ssw_status.  On failure a message is
+ * available from ssw_last_error() (thread-local).
+ *
+ * Output layout (identical to the reference):
+ *   output       uint8 [num_rows, physical_n/2]; element 2j in the low nibble,
+ *                element 2j+1 in the high nibble of byte j (E2M1 codes).
+ *   output_scale swizzled: bytes of [round_up(num_rows,128), round_up(physical_n/16,4)]
+ *                in the CUTLASS 128x4 scale-factor layout; linear: [num_rows,
+ *                physical_n/16].  Bytes of the swizzled padding (rows >= num_rows,
+ *                block columns >= physical_n/16) are left untouched.
+ *   input_scale  one float on the device: the multiplier 6*fp8_max/amax that
+ *                the reference calls "global_scale_inv".
+ */
+#ifndef SCALESWEEP_B200_H_
+#define SCALESWEEP_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SSW_ABI_VERSION 1
+
+typedef enum {
+  SSW_OK = 0,
+  SSW_ERR_INVALID_ARGUMENT = 1, /* shape, dtype, alignment or pointer problem */
+  SSW_ERR_UNSUPPORTED = 2,      /* valid request this build does not implement */
+  SSW_ERR_CUDA = 3,             /* a CUDA runtime call failed (launch, attribute) */
+  SSW_ERR_TIMEOUT = 4           /* a bounded device-side wait gave up */
+} ssw_status;
+
+typedef enum { SSW_DTYPE_BF16 = 0, SSW_DTYPE_F16 = 1 } ssw_dtype;
+
+/* Library / error reporting. */
+int ssw_abi_version(void);
+const char* ssw_status_string(int status);
+const char* ssw_last_error(void);
+
+/*
+ * Scale-sweep MSE quantizer, "scalesweep_mse" backend: round-to-nearest base
+ * code, 11 candidates [base-3, base+7] clamped to [1,126], fp32 SSE as a
+ * sequential FMA chain over elements 0..15, strict '<' argmin (ties -> lowest
+ * candidate).  physical_n >= n: block columns past n/16 are quantized as zero
+ * blocks (the reference's padded_n path).
+ * Replaces bench_kernel/scalesweep_mse_nvfp4_utils.py:462-477
+ * (scalesweep_mse_nvfp4_quant_out) and its launcher :424-459.
+ */
+int ssw_scalesweep_mse_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows,
+                                       int64_t n, int64_t physical_n, const float* input_scale,
+                                       uint8_t* output, uint8_t* output_scale,
+                                       int is_sf_swizzled_layout, void* stream);
+
+/*
+ * Full-range "scalesweep_mse128": candidates are every E4M3 code 1..126.
+ * Replaces bench_kernel/scalesweep_mse_nvfp4_utils.py:480-495
+ * (scalesweep_mse128_nvfp4_quant_out).
+ */
+int ssw_scalesweep_mse128_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows,
+                                          int64_t n, int64_t physical_n,
+                                          const float* input_scale, uint8_t* output,
+                                          uint8_t* output_scale, int is_sf_swizzled_layout,
+                                          void* stream);
+
+/*
+ * "scalesweep_mse_reference" variant: base code rounded DOWN (largest E4M3
+ * <= amax/6), SSE as the pairwise tree ((s01+s23)+(s45+s67))+((s89+sAB)+(sCD+sEF)).
+ * physical_n must equal n (SSW_ERR_INVALID_ARGUMENT otherwise), as in the reference.
+ * Replaces bench_kernel/scalesweep_mse_reference_nvfp4_utils.py:412-445
+ * (scalesweep_mse_nvfp4_quant_out).
+ */
+int ssw_scalesweep_mse_reference_nvfp4_quant_out(const void* input, int input_dtype,
+                                                 int64_t num_rows, int64_t n, int64_t physical_n,
+                                                 const float* input_scale, uint8_t* output,
+                                                 uint8_t* output_scale,
+                                                 int is_sf_swizzled_layout, void* stream);
+
+/*
+ * Plain round-to-nearest NVFP4 comparator: scale code = clamp(e4m3(amax/6),1,126),
+ * codes = e2m1(v / scale), same layouts.  Stands in for vLLM's
+ * scaled_fp4_quant.out that bench_kernel/custom.py:24-31 dispatches "cutlass"/"vllm" to.
+ */
+int ssw_rtn_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows, int64_t n,
+                            int64_t physical_n, const float* input_scale, uint8_t* output,
+                            uint8_t* output_scale, int is_sf_swizzled_layout, void* stream);
+
+/*
+ * Per-tensor |x| maximum.  Writes max|x| (NaN if any element is NaN, like
+ * torch's x.abs().max()) to amax_out[0].  `workspace` is caller-provided device
+ * scratch of at least ssw_absmax_workspace_bytes() bytes, 4-byte aligned; it
+ * is reset by the call itself (calls sharing a workspace must not overlap).
+ * Replaces the x.abs().max() half of bench_kernel/test_kernel_latency.py:65-70.
+ */
+int64_t ssw_absmax_workspace_bytes(void);
+int ssw_absmax(const void* input, int input_dtype, int64_t numel, float* amax_out,
+               void* workspace, void* stream);
+
+/*
+ * input_scale = (fp8_max * 6) / amax, evaluated as torch evaluates
+ * `(fp8_max * 6.0) / amax_tensor`: reciprocal(amax) rounded, then times
+ * fp8_max*6 rounded.  amax and out are device floats.
+ * Replaces the division of bench_kernel/test_kernel_latency.py:65-70.
+ */
+int ssw_global_scale_from_amax(const float* amax, float fp8_max, float* input_scale_out,
+                               void* stream);
+
+/*
+ * Fused single-launch amax + input_scale: one pass over `input` (the last CTA
+ * to finish turns the reduced amax into the scale), result in
+ * input_scale_out[0] and, if amax_out is non-NULL, amax in amax_out[0].
+ * Same workspace rules as ssw_absmax.
+ * Replaces bench_kernel/test_kernel_latency.py:65-75 (global_scale_inv).
+ */
+int ssw_global_scale_inv(const void* input, int input_dtype, int64_t numel, float fp8_max,
+                         float* input_scale_out, float* amax_out, void* workspace,
+                         void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SCALESWEEP_B200_H_ */

@@ -1,0 +1,291 @@
+/*
+ * CPU ORACLE -- test infrastructure only.
+ *
+ * A plain-C restatement of the reference's scale-sweep NVFP4 activation
+ * quantizer, used by tests/ and by bench.py's CPU-baseline leg as the checker.
+ * It is never linked into, loaded by, or called from the product library.
+ *
+ * Restated algorithms (reference paths are relative to the reference repo):
+ *   K1 "scalesweep_mse"           bench_kernel/scalesweep_mse_nvfp4_utils.py:302-421
+ *       helpers                    :23-43 (swizzle), :46-89 (pack), :92-176 (chain SSE),
+ *                                  :179-206 (x = v*inv, mse = sse*s^2), :209-229 (amax),
+ *                                  :232-270 (load + normalise)
+ *       host launch                :424-459 (block counts, Kpad, padded_n)
+ *       full-range "mse128" mode   :360-361, :452-454
+ *   K2 "scalesweep_mse_reference" bench_kernel/scalesweep_mse_reference_nvfp4_utils.py:301-409
+ *       round-down base            :347-351
+ *       pairwise tree SSE          :91-143
+ *       swizzle                    :18-41
+ *   global scale                   bench_kernel/test_kernel_latency.py:65-75
+ *       ((fp8_max*6) / amax is torch's Tensor.__rdiv__ = reciprocal(amax) * scalar)
+ *   RTN comparator                 single candidate at the window's base code
+ *
+ * Hardware semantics the reference's inline PTX and Triton casts rely on,
+ * pinned on a B200 with a probe and restated here:
+ *   cvt.rn.satfinite.e2m1x2.f32 : nearest-even on {0,.5,1,1.5,2,3,4,6}, saturate
+ *                                 at 6, sign kept (-0 too), NaN (any sign) -> +6.
+ *   fp32 -> float8e4nv          : nearest-even, saturate finite (>448 -> 448,
+ *                                 inf -> 448), NaN (any sign) -> 0x7F.
+ *   1.0f / e4m3 value           : Triton's '/' equals the IEEE quotient for
+ *                                 every one of the 128 E4M3 codes.
+ *   tl.maximum                  : returns the non-NaN operand (fmaxf).
+ *
+ * Build with strict IEEE binary32: -O2 -fno-fast-math -ffp-contract=off.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+#include <stdlib.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+enum { ORC_MSE = 0, ORC_REFERENCE = 1 };
+enum { ORC_WINDOW = 0, ORC_FULL_RANGE = 1, ORC_RTN = 2 };
+enum { ORC_BF16 = 0, ORC_F16 = 1 };
+
+#define LOWER_BOUND (-3)
+#define NUM_WINDOW 11
+#define MAX_SCALE_RAW 126
+
+static float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+
+static float bf16_to_f32(uint16_t h) { return u2f((uint32_t)h << 16); }
+
+static float f16_to_f32(uint16_t h) {
+  uint32_t sign = (uint32_t)(h >> 15) << 31;
+  uint32_t e = (h >> 10) & 0x1F, m = h & 0x3FF;
+  if (e == 0) {
+    float v = ldexpf((float)m, -24);  /* exact: m < 2^10 */
+    return (h >> 15) ? -v : v;
+  }
+  if (e == 31) return u2f(sign | 0x7F800000u | (m << 13));
+  return u2f(sign | ((e + 112) << 23) | (m << 13));
+}
+
+static float load_elem(const uint16_t* p, int dtype) {
+  return dtype == ORC_F16 ? f16_to_f32(*p) : bf16_to_f32(*p);
+}
+
+/* ---- E2M1 ---------------------------------------------------------------- */
+static const float kE2M1[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+
+static uint8_t e2m1_encode(float x) {
+  if (isnan(x)) return 0x7;
+  float a = fabsf(x);
+  uint8_t c;
+  if (a <= 0.25f) c = 0;
+  else if (a < 0.75f) c = 1;
+  else if (a <= 1.25f) c = 2;
+  else if (a < 1.75f) c = 3;
+  else if (a <= 2.5f) c = 4;
+  else if (a < 3.5f) c = 5;
+  else if (a <= 5.0f) c = 6;
+  else c = 7;
+  return (uint8_t)(c | (signbit(x) ? 8 : 0));
+}
+
+static float e2m1_decode(uint8_t nib) {
+  float v = kE2M1[nib & 7];
+  return (nib & 8) ? -v : v;
+}
+
+/* ---- E4M3 (fn) ----------------------------------------------------------- */
+static float e4m3_decode(uint8_t raw) {
+  int e = (raw >> 3) & 0xF, m = raw & 7;
+  float mag;
+  if ((raw & 0x7F) == 0x7F) return NAN;
+  if (e == 0) mag = ldexpf((float)m, -9);
+  else mag = ldexpf((float)(8 + m), e - 10);
+  return (raw & 0x80) ? -mag : mag;
+}
+
+/* nearest-even, saturating finite; NaN -> 0x7F */
+static uint8_t e4m3_encode(float x) {
+  if (isnan(x)) return 0x7F;
+  uint8_t sign = signbit(x) ? 0x80 : 0;
+  double a = fabs((double)x);
+  uint8_t code;
+  if (a > 448.0) {
+    code = 0x7E;
+  } else if (a < 0.015625) { /* below 2^-6: subnormal grid 2^-9 */
+    code = (uint8_t)nearbyint(a * 512.0);   /* default rounding: nearest-even */
+  } else {
+    int e;
+    double fr = frexp(a, &e);            /* a = fr * 2^e, fr in [0.5, 1) */
+    double m = nearbyint((fr * 2.0 - 1.0) * 8.0);
+    int E = e - 1;
+    if (m >= 8.0) { m = 0.0; E += 1; }
+    int c = (E + 7) * 8 + (int)m;
+    code = (uint8_t)(c > 0x7E ? 0x7E : c);
+  }
+  return (uint8_t)(code | sign);
+}
+
+/* ---- CUTLASS 128x4 scale-factor swizzle ---------------------------------- */
+int64_t orc_swizzled_offset(int64_t row, int64_t col, int64_t bpc_pad) {
+  return (row >> 7) * (bpc_pad * 128) + (col >> 2) * 512 + (row & 31) * 16 +
+         ((row & 127) >> 5) * 4 + (col & 3);
+}
+
+/* ---- one 16-element block ------------------------------------------------ */
+static float block_sse_chain(const float* v, float inv) {
+  /* scalesweep_mse_nvfp4_utils.py:92-176: d0^2, then fma(d1,d1,.), fma(d2,d2,.) ... */
+  float acc = 0.0f;
+  for (int j = 0; j < 16; j += 2) {
+    float x0 = v[j] * inv, x1 = v[j + 1] * inv;
+    float d0 = e2m1_decode(e2m1_encode(x0)) - x0;
+    float d1 = e2m1_decode(e2m1_encode(x1)) - x1;
+    if (j == 0) acc = d0 * d0;
+    else acc = fmaf(d0, d0, acc);
+    acc = fmaf(d1, d1, acc);
+  }
+  return acc;
+}
+
+static float block_sse_tree(const float* v, float inv) {
+  /* scalesweep_mse_reference_nvfp4_utils.py:91-143 */
+  float s[8];
+  for (int k = 0; k < 8; ++k) {
+    float x0 = v[2 * k] * inv, x1 = v[2 * k + 1] * inv;
+    float d0 = e2m1_decode(e2m1_encode(x0)) - x0;
+    float d1 = e2m1_decode(e2m1_encode(x1)) - x1;
+    float p = d0 * d0;
+    s[k] = fmaf(d1, d1, p);
+  }
+  return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
+}
+
+static uint8_t clamp_raw(int r) {
+  return (uint8_t)(r < 1 ? 1 : (r > MAX_SCALE_RAW ? MAX_SCALE_RAW : r));
+}
+
+/* Quantize one block of 16 normalised values; returns the scale byte and
+ * writes the 8 packed code bytes (even element in the low nibble). */
+static uint8_t quant_block(const float* v, int variant, int mode, uint8_t* code_out) {
+  float amax = 0.0f;
+  {
+    /* scalesweep_mse_nvfp4_utils.py:209-229 -- pairwise max tree */
+    float m[8];
+    for (int k = 0; k < 8; ++k) m[k] = fmaxf(fabsf(v[2 * k]), fabsf(v[2 * k + 1]));
+    float m01 = fmaxf(m[0], m[1]), m23 = fmaxf(m[2], m[3]);
+    float m45 = fmaxf(m[4], m[5]), m67 = fmaxf(m[6], m[7]);
+    amax = fmaxf(fmaxf(m01, m23), fmaxf(m45, m67));
+  }
+  const float sixth = (float)(1.0 / 6.0);
+  float base = amax * sixth;
+  uint8_t base_fp8 = e4m3_encode(base);
+  int base_raw = base_fp8;
+  if (variant == ORC_REFERENCE) {
+    /* scalesweep_mse_reference_nvfp4_utils.py:347-351 */
+    base_raw -= (e4m3_decode(base_fp8) > base) ? 1 : 0;
+  }
+
+  float best = INFINITY;
+  uint8_t best_raw = 0;
+  if (mode == ORC_RTN) {
+    /* round-to-nearest comparator: the window's base code, no sweep */
+    best_raw = clamp_raw(base_raw);
+  } else {
+    int n_cand = mode == ORC_FULL_RANGE ? MAX_SCALE_RAW : NUM_WINDOW;
+    for (int i = 0; i < n_cand; ++i) {
+      uint8_t raw = mode == ORC_FULL_RANGE ? (uint8_t)(i + 1)
+                                           : clamp_raw(base_raw + LOWER_BOUND + i);
+      float s = e4m3_decode(raw);
+      float inv = 1.0f / s;
+      float sse = variant == ORC_REFERENCE ? block_sse_tree(v, inv) : block_sse_chain(v, inv);
+      float mse = sse * (s * s);
+      /* strict '<': NaN never wins, ties keep the lowest index (:380-382) */
+      if (mse < best) { best = mse; best_raw = raw; }
+    }
+  }
+
+  float inv = 1.0f / e4m3_decode(best_raw);
+  for (int k = 0; k < 8; ++k) {
+    uint8_t lo = e2m1_encode(v[2 * k] * inv);
+    uint8_t hi = e2m1_encode(v[2 * k + 1] * inv);
+    code_out[k] = (uint8_t)(lo | (hi << 4));
+  }
+  return best_raw;
+}
+
+/*
+ * input      : [m, n_in] bf16/f16 bits, row-major contiguous
+ * n_out      : physical columns of the output (n_in, or padded_n); multiple of 16
+ * codes      : [m, n_out/2] bytes
+ * scales     : swizzled: [round_up(m,128), round_up(n_out/16,4)] bytes
+ *              linear:   [m, n_out/16] bytes
+ * Returns 0, or -1 for bad arguments.
+ */
+int orc_quantize(const uint16_t* input, int dtype, int64_t m, int64_t n_in, int64_t n_out,
+                 float gsi, uint8_t* codes, uint8_t* scales, int swizzled, int variant,
+                 int mode, int nthreads) {
+  if (m < 0 || n_in < 0 || n_out < n_in || (n_in % 16) || (n_out % 16)) return -1;
+  const int64_t bpc_in = n_in / 16, bpc_out = n_out / 16;
+  const int64_t bpc_pad = (bpc_out + 3) / 4 * 4;
+  const int64_t nblocks = m * bpc_out;
+#ifdef _OPENMP
+  if (nthreads <= 0) nthreads = omp_get_max_threads();
+#pragma omp parallel for num_threads(nthreads) schedule(static)
+#else
+  (void)nthreads;
+#endif
+  for (int64_t b = 0; b < nblocks; ++b) {
+    int64_t row = b / bpc_out, col = b % bpc_out;
+    float v[16];
+    for (int j = 0; j < 16; ++j) {
+      float x = col < bpc_in ? load_elem(input + (row * bpc_in + col) * 16 + j, dtype) : 0.0f;
+      v[j] = x * gsi;
+    }
+    uint8_t sc = quant_block(v, variant, mode, codes + b * 8);
+    int64_t off = swizzled ? orc_swizzled_offset(row, col, bpc_pad) : b;
+    scales[off] = sc;
+  }
+  return 0;
+}
+
+/* max |x| over the tensor (exact; NaN ignored unless every element is NaN). */
+float orc_absmax(const uint16_t* input, int dtype, int64_t count, int nthreads) {
+  float best = 0.0f;
+  int any_num = count == 0;
+#ifdef _OPENMP
+  if (nthreads <= 0) nthreads = omp_get_max_threads();
+#pragma omp parallel for num_threads(nthreads) reduction(max : best) reduction(| : any_num)
+#else
+  (void)nthreads;
+#endif
+  for (int64_t i = 0; i < count; ++i) {
+    float a = fabsf(load_elem(input + i, dtype));
+    if (!isnan(a)) { any_num |= 1; if (a > best) best = a; }
+  }
+  return any_num ? best : NAN;
+}
+
+/* torch: (fp8_max * 6.0) / amax.float()  ==  reciprocal(amax) * (fp8_max*6) */
+float orc_global_scale_inv(float amax, float fp8_max_times_6) {
+  float r = 1.0f / amax;
+  return r * fp8_max_times_6;
+}
+
+/* Dequantize NVFP4 (swizzled scales) to float: out[r, c] = e2m1 * e4m3. */
+int orc_dequantize(const uint8_t* codes, const uint8_t* scales, int64_t m, int64_t n,
+                   int swizzled, float* out) {
+  if (n % 16) return -1;
+  const int64_t bpc = n / 16, bpc_pad = (bpc + 3) / 4 * 4;
+  for (int64_t r = 0; r < m; ++r)
+    for (int64_t c = 0; c < n; ++c) {
+      uint8_t byte = codes[r * (n / 2) + c / 2];
+      uint8_t nib = (c & 1) ? (byte >> 4) : (byte & 0xF);
+      int64_t blk = c / 16;
+      int64_t off = swizzled ? orc_swizzled_offset(r, blk, bpc_pad) : r * bpc + blk;
+      out[r * n + c] = e2m1_decode(nib) * e4m3_decode(scales[off]);
+    }
+  return 0;
+}
+
+/* Exposed for unit tests of the primitive conversions. */
+uint8_t orc_e2m1_encode(float x) { return e2m1_encode(x); }
+uint8_t orc_e4m3_encode(float x) { return e4m3_encode(x); }
+float orc_e4m3_decode(uint8_t r) { return e4m3_decode(r); }
+uint32_t orc_f32_bits(float x) { return f2u(x); }

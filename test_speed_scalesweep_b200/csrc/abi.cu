@@ -1,0 +1,223 @@
+// C ABI of the scale-sweep NVFP4 library: argument validation, launch-shape
+// selection and error reporting.  Declarations and contracts live in
+// include/scalesweep_b200.h.
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include <cuda_runtime.h>
+
+#include "../../include/scalesweep_b200.h"
+#include "quant.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(SSW_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int device_sms(int* sms) {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) {
+    *sms = cache[dev];
+    return SSW_OK;
+  }
+  int v = 0;
+  e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  if (dev >= 0 && dev < 64) cache[dev] = v;
+  *sms = v;
+  return SSW_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int quant_out(const char* name, int variant, int mode, const void* input, int input_dtype,
+              int64_t num_rows, int64_t n, int64_t physical_n, const float* input_scale,
+              uint8_t* output, uint8_t* output_scale, int swizzled, void* stream) {
+  g_last_error.clear();
+  if (input_dtype != SSW_DTYPE_BF16 && input_dtype != SSW_DTYPE_F16)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: input dtype must be bf16 or f16 (got %d)", name,
+                input_dtype);
+  if (num_rows < 0 || n < 0 || physical_n < 0)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: negative size", name);
+  if (n % 16)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: the last input dimension must be a multiple of 16 (got %lld)",
+                name, (long long)n);
+  if (physical_n % 16)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: padded_n must be a multiple of 16 (got %lld)", name,
+                (long long)physical_n);
+  if (physical_n < n)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: padded_n (%lld) must be >= n (%lld)", name,
+                (long long)physical_n, (long long)n);
+  if (variant == ssw::kVariantReference && physical_n != n)
+    return fail(SSW_ERR_INVALID_ARGUMENT,
+                "%s: The reference ScaleSweep kernel does not support padded_n different from the "
+                "input width.",
+                name);
+  const uint64_t bpc_out = (uint64_t)physical_n / 16, bpc_in = (uint64_t)n / 16;
+  const uint64_t nblocks = (uint64_t)num_rows * bpc_out;
+  if (nblocks == 0) return SSW_OK;
+  if (nblocks >= (1ull << 32) || (uint64_t)num_rows >= (1ull << 31))
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: %llu blocks exceed the 2^32 per-call limit", name,
+                (unsigned long long)nblocks);
+  if (!output || !output_scale || !input_scale || (bpc_in > 0 && !input))
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (!aligned(input, 2) || !aligned(input_scale, 4))
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: misaligned input or input_scale pointer", name);
+
+  ssw::QuantParams p;
+  p.input = static_cast<const uint16_t*>(input);
+  p.input_scale = input_scale;
+  p.output = output;
+  p.output_scale = output_scale;
+  p.nblocks = nblocks;
+  p.bpc_in = (uint32_t)bpc_in;
+  p.bpc_out = (uint32_t)bpc_out;
+  p.bpc_pad = (uint32_t)((bpc_out + 3) / 4 * 4);
+  p.swizzled = swizzled ? 1 : 0;
+  p.scale_word_stores = (bpc_out % 4 == 0) && aligned(output_scale, 4);
+  const bool vec = aligned(input, 32) && aligned(output, 8);
+
+  int sms = 0;
+  int st = device_sms(&sms);
+  if (st != SSW_OK) return st;
+  const int grid = ssw::quant_grid_size(nblocks, sms);
+  cudaError_t e = ssw::launch_quant(p, variant, mode, input_dtype, vec, grid,
+                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, name);
+  return SSW_OK;
+}
+
+int amax_common(const char* name, const void* input, int input_dtype, int64_t numel,
+                float fp8_max, float* scale_out, float* amax_out, void* workspace,
+                void* stream) {
+  g_last_error.clear();
+  if (input_dtype != SSW_DTYPE_BF16 && input_dtype != SSW_DTYPE_F16)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: input dtype must be bf16 or f16", name);
+  if (numel <= 0)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: the maximum of an empty tensor is undefined", name);
+  if (!input || !workspace || (!scale_out && !amax_out))
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (!aligned(input, 2) || !aligned(workspace, 4))
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: misaligned input or workspace", name);
+  int sms = 0;
+  int st = device_sms(&sms);
+  if (st != SSW_OK) return st;
+  ssw::AmaxParams p;
+  p.input = static_cast<const uint16_t*>(input);
+  p.numel = (uint64_t)numel;
+  p.workspace = static_cast<uint32_t*>(workspace);
+  p.amax_out = amax_out;
+  p.scale_out = scale_out;
+  p.fp8_max_times_6 = fp8_max * 6.0f;
+  const bool vec = aligned(input, 32);
+  cudaError_t e = ssw::launch_amax(p, input_dtype, vec, ssw::amax_grid_size(p.numel, sms),
+                                   static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, name);
+  return SSW_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ssw_abi_version(void) { return SSW_ABI_VERSION; }
+
+const char* ssw_status_string(int status) {
+  switch (status) {
+    case SSW_OK: return "ok";
+    case SSW_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case SSW_ERR_UNSUPPORTED: return "unsupported";
+    case SSW_ERR_CUDA: return "CUDA error";
+    case SSW_ERR_TIMEOUT: return "device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* ssw_last_error(void) { return g_last_error.c_str(); }
+
+int ssw_scalesweep_mse_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows,
+                                       int64_t n, int64_t physical_n, const float* input_scale,
+                                       uint8_t* output, uint8_t* output_scale,
+                                       int is_sf_swizzled_layout, void* stream) {
+  return quant_out("scalesweep_mse_nvfp4_quant_out", ssw::kVariantMse, ssw::kModeWindow, input,
+                   input_dtype, num_rows, n, physical_n, input_scale, output, output_scale,
+                   is_sf_swizzled_layout, stream);
+}
+
+int ssw_scalesweep_mse128_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows,
+                                          int64_t n, int64_t physical_n,
+                                          const float* input_scale, uint8_t* output,
+                                          uint8_t* output_scale, int is_sf_swizzled_layout,
+                                          void* stream) {
+  return quant_out("scalesweep_mse128_nvfp4_quant_out", ssw::kVariantMse, ssw::kModeFullRange,
+                   input, input_dtype, num_rows, n, physical_n, input_scale, output, output_scale,
+                   is_sf_swizzled_layout, stream);
+}
+
+int ssw_scalesweep_mse_reference_nvfp4_quant_out(const void* input, int input_dtype,
+                                                 int64_t num_rows, int64_t n, int64_t physical_n,
+                                                 const float* input_scale, uint8_t* output,
+                                                 uint8_t* output_scale,
+                                                 int is_sf_swizzled_layout, void* stream) {
+  return quant_out("scalesweep_mse_reference_nvfp4_quant_out", ssw::kVariantReference,
+                   ssw::kModeWindow, input, input_dtype, num_rows, n, physical_n, input_scale,
+                   output, output_scale, is_sf_swizzled_layout, stream);
+}
+
+int ssw_rtn_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows, int64_t n,
+                            int64_t physical_n, const float* input_scale, uint8_t* output,
+                            uint8_t* output_scale, int is_sf_swizzled_layout, void* stream) {
+  return quant_out("rtn_nvfp4_quant_out", ssw::kVariantMse, ssw::kModeRtn, input, input_dtype,
+                   num_rows, n, physical_n, input_scale, output, output_scale,
+                   is_sf_swizzled_layout, stream);
+}
+
+int64_t ssw_absmax_workspace_bytes(void) { return 8; }
+
+int ssw_absmax(const void* input, int input_dtype, int64_t numel, float* amax_out,
+               void* workspace, void* stream) {
+  return amax_common("absmax", input, input_dtype, numel, 0.0f, nullptr, amax_out, workspace,
+                     stream);
+}
+
+int ssw_global_scale_from_amax(const float* amax, float fp8_max, float* input_scale_out,
+                               void* stream) {
+  g_last_error.clear();
+  if (!amax || !input_scale_out)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "global_scale_from_amax: null pointer");
+  cudaError_t e = ssw::launch_scale_from_amax(amax, fp8_max * 6.0f, input_scale_out,
+                                              static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "global_scale_from_amax");
+  return SSW_OK;
+}
+
+int ssw_global_scale_inv(const void* input, int input_dtype, int64_t numel, float fp8_max,
+                         float* input_scale_out, float* amax_out, void* workspace,
+                         void* stream) {
+  if (!input_scale_out) {
+    g_last_error = "global_scale_inv: null input_scale_out";
+    return SSW_ERR_INVALID_ARGUMENT;
+  }
+  return amax_common("global_scale_inv", input, input_dtype, numel, fp8_max, input_scale_out,
+                     amax_out, workspace, stream);
+}
+
+}  // extern "C"

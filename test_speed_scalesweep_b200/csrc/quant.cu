@@ -1,0 +1,311 @@
+// Fused scale-sweep NVFP4 block quantizer for sm_100a.
+//
+// One thread owns one 16-element block (32 bytes of bf16/f16 input, 8 bytes
+// of codes, 1 scale byte).  A warp covers 32 consecutive blocks, so its input
+// load is one 1 KiB contiguous 256-bit-per-lane transaction and its code store
+// one 256 B contiguous transaction; four neighbouring lanes gather their scale
+// bytes into one 32-bit store in the swizzled (or linear) scale layout.
+//
+// The candidate sweep is the hot loop.  Two candidates are evaluated side by
+// side so that the normalisation multiply and the squared-error FMA run as
+// packed f32x2 instructions (one issue slot for two lanes of work) and the
+// E2M1 round trip's decode+subtract is a single mixed-precision
+// sub.rn.f32.f16.  Summation order and rounding are exactly the reference's:
+//   "mse"       : acc = d0*d0; acc = fma(d1,d1,acc); ... fma(d15,d15,acc)
+//                 (bench_kernel/scalesweep_mse_nvfp4_utils.py:92-176)
+//   "reference" : s_k = fma(d_{2k+1}, d_{2k+1}, d_{2k}*d_{2k}),
+//                 ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7))
+//                 (bench_kernel/scalesweep_mse_reference_nvfp4_utils.py:91-143)
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "ptx.cuh"
+#include "quant.cuh"
+
+namespace ssw {
+
+namespace {
+
+constexpr int kThreads = 256;  // the shared tables below rely on 256 threads
+constexpr int kLower = -3;       // bench_kernel/scalesweep_mse_nvfp4_utils.py:17
+constexpr int kWindow = 11;      // UPPER_BOUND - LOWER_BOUND + 1 (:17-18, :452-454)
+constexpr int kMaxRaw = 126;     // REF_MAX_SCALE_RAW (:20)
+
+struct ScaleEntry {
+  float inv;  // 1 / s, IEEE (equals the reference's Triton 1.0 / s for every code)
+  float s2;   // s * s (exact)
+};
+
+__device__ __forceinline__ int clamp_raw(int r) { return r < 1 ? 1 : (r > kMaxRaw ? kMaxRaw : r); }
+
+// Squared error of the 16 values for two candidate reciprocals at once.
+// Returns {sse_a, sse_b} packed.
+template <int kVariant>
+__device__ __forceinline__ uint64_t sse_pair(const uint64_t (&vp)[8], float inv_a, float inv_b) {
+  const uint64_t ia = pack2(inv_a, inv_a), ib = pack2(inv_b, inv_b);
+  if constexpr (kVariant == kVariantMse) {
+    uint64_t acc = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float xa0, xa1, xb0, xb1, da0, da1, db0, db1;
+      unpack2(mul2(vp[k], ia), xa0, xa1);
+      unpack2(mul2(vp[k], ib), xb0, xb1);
+      e2m1_delta2(xa0, xa1, da0, da1);
+      e2m1_delta2(xb0, xb1, db0, db1);
+      const uint64_t d0 = pack2(da0, db0), d1 = pack2(da1, db1);
+      acc = (k == 0) ? mul2(d0, d0) : fma2(d0, d0, acc);
+      acc = fma2(d1, d1, acc);
+    }
+    return acc;
+  } else {
+    uint64_t s[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float xa0, xa1, xb0, xb1, da0, da1, db0, db1;
+      unpack2(mul2(vp[k], ia), xa0, xa1);
+      unpack2(mul2(vp[k], ib), xb0, xb1);
+      e2m1_delta2(xa0, xa1, da0, da1);
+      e2m1_delta2(xb0, xb1, db0, db1);
+      const uint64_t d0 = pack2(da0, db0), d1 = pack2(da1, db1);
+      s[k] = fma2(d1, d1, mul2(d0, d0));
+    }
+    return add2(add2(add2(s[0], s[1]), add2(s[2], s[3])), add2(add2(s[4], s[5]), add2(s[6], s[7])));
+  }
+}
+
+// Single-candidate squared error (the odd candidate of the 11-wide window).
+template <int kVariant>
+__device__ __forceinline__ float sse_one(const uint64_t (&vp)[8], float inv) {
+  const uint64_t i2 = pack2(inv, inv);
+  if constexpr (kVariant == kVariantMse) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float x0, x1, d0, d1;
+      unpack2(mul2(vp[k], i2), x0, x1);
+      e2m1_delta2(x0, x1, d0, d1);
+      acc = (k == 0) ? mul_rn(d0, d0) : fma_rn(d0, d0, acc);
+      acc = fma_rn(d1, d1, acc);
+    }
+    return acc;
+  } else {
+    float s[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float x0, x1, d0, d1;
+      unpack2(mul2(vp[k], i2), x0, x1);
+      e2m1_delta2(x0, x1, d0, d1);
+      s[k] = fma_rn(d1, d1, mul_rn(d0, d0));
+    }
+    return add_rn(add_rn(add_rn(s[0], s[1]), add_rn(s[2], s[3])),
+                  add_rn(add_rn(s[4], s[5]), add_rn(s[6], s[7])));
+  }
+}
+
+__device__ __forceinline__ void consider(float mse, int raw, float& best, int& best_raw) {
+  // strict '<': NaN never wins and ties keep the earlier (lower-index) candidate
+  if (mse < best) {
+    best = mse;
+    best_raw = raw;
+  }
+}
+
+__device__ __forceinline__ void consider_pair(uint64_t sse, float s2a, float s2b, int ra, int rb,
+                                              float& best, int& best_raw) {
+  float ma, mb;
+  unpack2(mul2(sse, pack2(s2a, s2b)), ma, mb);
+  consider(ma, ra, best, best_raw);
+  consider(mb, rb, best, best_raw);
+}
+
+template <int kVariant, int kMode, int kDType, bool kVec>
+__global__ void __launch_bounds__(kThreads) quant_kernel(QuantParams p) {
+  // Per-code table: reciprocal and square of every E4M3 scale (codes 0..127),
+  // and the signed value of every byte (the reference variant compares the
+  // base code's value with amax/6).
+  __shared__ ScaleEntry tab[128];
+  __shared__ float tab_s[256];
+  {
+    const uint32_t c = threadIdx.x;  // kThreads == 256
+    const float mag = e4m3_value(c & 0x7F);
+    tab_s[c] = (c & 0x80) ? -mag : mag;
+    if (c < 128) {
+      float inv;
+      asm("rcp.rn.f32 %0, %1;" : "=f"(inv) : "f"(mag));
+      tab[c] = ScaleEntry{inv, mul_rn(mag, mag)};
+    }
+  }
+  __syncthreads();
+
+  const float gsi = __ldg(p.input_scale);
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t warp = ((uint64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
+  const uint64_t nwarps = ((uint64_t)gridDim.x * kThreads) >> 5;
+  const uint32_t bpc_out = p.bpc_out, bpc_in = p.bpc_in;
+
+  for (uint64_t first = warp * 32; first < p.nblocks; first += nwarps * 32) {
+    const uint64_t b = first + lane;
+    const bool valid = b < p.nblocks;
+    const uint32_t bb = (uint32_t)b;
+    const uint32_t row = valid ? bb / bpc_out : 0;
+    const uint32_t col = valid ? bb - row * bpc_out : 0;
+    const bool has_data = valid && col < bpc_in;
+
+    // ---- load + normalise (bench_kernel/scalesweep_mse_nvfp4_utils.py:232-270)
+    uint32_t w[8];
+    if (has_data) {
+      const uint16_t* src = p.input + ((uint64_t)row * bpc_in + col) * 16;
+      if constexpr (kVec) {
+        ld_block_v8(src, w);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          w[j] = (uint32_t)__ldg(src + 2 * j) | ((uint32_t)__ldg(src + 2 * j + 1) << 16);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = 0u;
+    }
+    uint64_t vp[8];
+    const uint64_t g2 = pack2(gsi, gsi);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float lo, hi;
+      if constexpr (kDType == kDTypeBF16) {
+        lo = __uint_as_float(w[j] << 16);
+        hi = __uint_as_float(w[j] & 0xFFFF0000u);
+      } else {
+        lo = __half2float(__ushort_as_half((unsigned short)(w[j] & 0xFFFF)));
+        hi = __half2float(__ushort_as_half((unsigned short)(w[j] >> 16)));
+      }
+      vp[j] = mul2(pack2(lo, hi), g2);
+    }
+
+    // ---- block amax (:209-229) and base code (:353-354; reference :347-351)
+    float m[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float lo, hi;
+      unpack2(vp[j], lo, hi);
+      m[j] = fmaxf(fabsf(lo), fabsf(hi));
+    }
+    const float amax = fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])),
+                             fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
+    const float base = mul_rn(amax, (float)(1.0 / 6.0));
+    int base_raw = (int)e4m3_code(base);  // 0..255
+    if constexpr (kVariant == kVariantReference) {
+      base_raw -= (tab_s[base_raw] > base) ? 1 : 0;
+    }
+
+    // ---- candidate sweep (:356-382)
+    int best_raw = 0;
+    if constexpr (kMode == kModeRtn) {
+      best_raw = clamp_raw(base_raw);
+    } else if constexpr (kMode == kModeWindow) {
+      float best = __uint_as_float(0x7F800000u);
+#pragma unroll
+      for (int i = 0; i + 1 < kWindow; i += 2) {
+        const int ra = clamp_raw(base_raw + kLower + i);
+        const int rb = clamp_raw(base_raw + kLower + i + 1);
+        const ScaleEntry ea = tab[ra], eb = tab[rb];
+        consider_pair(sse_pair<kVariant>(vp, ea.inv, eb.inv), ea.s2, eb.s2, ra, rb, best,
+                      best_raw);
+      }
+      {
+        const int r = clamp_raw(base_raw + kLower + kWindow - 1);
+        const ScaleEntry e = tab[r];
+        consider(mul_rn(sse_one<kVariant>(vp, e.inv), e.s2), r, best, best_raw);
+      }
+    } else {  // full range: every code 1..126 (:360-361)
+      float best = __uint_as_float(0x7F800000u);
+#pragma unroll 1
+      for (int r = 1; r <= kMaxRaw; r += 2) {
+        const ScaleEntry ea = tab[r], eb = tab[r + 1];
+        consider_pair(sse_pair<kVariant>(vp, ea.inv, eb.inv), ea.s2, eb.s2, r, r + 1, best,
+                      best_raw);
+      }
+    }
+
+    // ---- final codes with the chosen scale (:399-421)
+    const float inv = tab[best_raw].inv;
+    const uint64_t i2 = pack2(inv, inv);
+    float x[16];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) unpack2(mul2(vp[j], i2), x[2 * j], x[2 * j + 1]);
+    const uint32_t lo_word = e2m1x8(x[0], x[1], x[2], x[3], x[4], x[5], x[6], x[7]);
+    const uint32_t hi_word = e2m1x8(x[8], x[9], x[10], x[11], x[12], x[13], x[14], x[15]);
+    if (valid) {
+      if constexpr (kVec) {
+        st_v2(p.output + b * 8, lo_word, hi_word);
+      } else {
+        uint8_t* dst = p.output + b * 8;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          dst[j] = (uint8_t)(lo_word >> (8 * j));
+          dst[4 + j] = (uint8_t)(hi_word >> (8 * j));
+        }
+      }
+    }
+
+    // ---- scale store (:384-397), swizzle (:23-43)
+    uint64_t off;
+    if (p.swizzled) {
+      off = (uint64_t)(row >> 7) * ((uint64_t)p.bpc_pad * 128) + (uint64_t)(col >> 2) * 512 +
+            (row & 31) * 16 + ((row & 127) >> 5) * 4 + (col & 3);
+    } else {
+      off = b;
+    }
+    if (p.scale_word_stores) {
+      // bpc_out % 4 == 0: lanes 4j..4j+3 hold columns 4c..4c+3 of one row,
+      // which are four consecutive bytes in both layouts.
+      const uint32_t s0 = (uint32_t)best_raw;
+      const uint32_t s1 = __shfl_down_sync(0xFFFFFFFFu, s0, 1);
+      const uint32_t s2 = __shfl_down_sync(0xFFFFFFFFu, s0, 2);
+      const uint32_t s3 = __shfl_down_sync(0xFFFFFFFFu, s0, 3);
+      if (valid && (lane & 3) == 0)
+        *reinterpret_cast<uint32_t*>(p.output_scale + off) = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
+    } else if (valid) {
+      p.output_scale[off] = (uint8_t)best_raw;
+    }
+  }
+}
+
+template <int kVariant, int kMode, int kDType, bool kVec>
+cudaError_t launch_one(const QuantParams& p, int grid, cudaStream_t stream) {
+  quant_kernel<kVariant, kMode, kDType, kVec><<<grid, kThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <int kVariant, int kMode>
+cudaError_t launch_dtype(const QuantParams& p, int dtype, bool vec, int grid, cudaStream_t s) {
+  if (dtype == kDTypeBF16)
+    return vec ? launch_one<kVariant, kMode, kDTypeBF16, true>(p, grid, s)
+               : launch_one<kVariant, kMode, kDTypeBF16, false>(p, grid, s);
+  return vec ? launch_one<kVariant, kMode, kDTypeF16, true>(p, grid, s)
+             : launch_one<kVariant, kMode, kDTypeF16, false>(p, grid, s);
+}
+
+}  // namespace
+
+int quant_grid_size(uint64_t nblocks, int device_sms) {
+  // 8 warps per CTA, 32 blocks per warp per iteration; cap at 4 resident CTAs
+  // per SM and let the grid-stride loop cover the rest.
+  const uint64_t per_cta = (uint64_t)kThreads;
+  uint64_t need = (nblocks + per_cta - 1) / per_cta;
+  const uint64_t cap = (uint64_t)device_sms * 4;
+  if (need > cap) need = cap;
+  if (need < 1) need = 1;
+  return (int)need;
+}
+
+cudaError_t launch_quant(const QuantParams& p, int variant, int mode, int dtype, bool vec,
+                         int grid, cudaStream_t stream) {
+  if (variant == kVariantMse) {
+    if (mode == kModeWindow) return launch_dtype<kVariantMse, kModeWindow>(p, dtype, vec, grid, stream);
+    if (mode == kModeFullRange) return launch_dtype<kVariantMse, kModeFullRange>(p, dtype, vec, grid, stream);
+    return launch_dtype<kVariantMse, kModeRtn>(p, dtype, vec, grid, stream);
+  }
+  return launch_dtype<kVariantReference, kModeWindow>(p, dtype, vec, grid, stream);
+}
+
+}  // namespace ssw

@@ -1,0 +1,45 @@
+// Internal launch interface of the quantizer kernels (not part of the C ABI).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+namespace ssw {
+
+enum { kVariantMse = 0, kVariantReference = 1 };
+enum { kModeWindow = 0, kModeFullRange = 1, kModeRtn = 2 };
+enum { kDTypeBF16 = 0, kDTypeF16 = 1 };
+
+struct QuantParams {
+  const uint16_t* input;      // [rows, bpc_in*16] 16-bit floats
+  const float* input_scale;   // one float: 6*fp8_max/amax
+  uint8_t* output;            // [rows, bpc_out*8] packed codes
+  uint8_t* output_scale;      // swizzled or linear scale bytes
+  uint64_t nblocks;           // rows * bpc_out (< 2^32)
+  uint32_t bpc_in;            // input blocks per row  (n / 16)
+  uint32_t bpc_out;           // output blocks per row (physical_n / 16)
+  uint32_t bpc_pad;           // round_up(bpc_out, 4)
+  int swizzled;
+  int scale_word_stores;      // bpc_out % 4 == 0 and output_scale 4-byte aligned
+};
+
+int quant_grid_size(uint64_t nblocks, int device_sms);
+cudaError_t launch_quant(const QuantParams& p, int variant, int mode, int dtype, bool vec,
+                         int grid, cudaStream_t stream);
+
+// amax / global scale
+struct AmaxParams {
+  const uint16_t* input;
+  uint64_t numel;
+  uint32_t* workspace;  // [0] = max |x| bits, [1] = finished-CTA counter
+  float* amax_out;      // may be null (fused path)
+  float* scale_out;     // may be null (plain amax path)
+  float fp8_max_times_6;
+};
+int amax_grid_size(uint64_t numel, int device_sms);
+cudaError_t launch_amax(const AmaxParams& p, int dtype, bool vec, int grid, cudaStream_t stream);
+cudaError_t launch_scale_from_amax(const float* amax, float fp8_max_times_6, float* out,
+                                   cudaStream_t stream);
+
+}  // namespace ssw

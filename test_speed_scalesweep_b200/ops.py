@@ -1,0 +1,99 @@
+"""torch.library registration of the quantizer ops (functional + ``.out``) with
+fake (meta) implementations, so the ops work under torch.compile and inside
+CUDA graphs exactly like the ops the reference's vLLM fork registered
+(``torch.ops.vllm.scalesweep_mse_nvfp4_quant``, ...; the fake functions of
+``bench_kernel/scalesweep_mse_nvfp4_utils.py:546-572`` are their shape
+functions).
+
+Ops live in the ``scalesweep_b200`` namespace.  ``register_vllm_aliases()``
+additionally defines the same schemas under the ``vllm`` namespace for a
+vLLM build that looks them up there.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import scalesweep_mse_nvfp4_utils as mse
+from . import scalesweep_mse_reference_nvfp4_utils as mse_ref
+
+NAMESPACE = "scalesweep_b200"
+
+_FUNCTIONAL = ("(Tensor input, Tensor input_scale, bool is_sf_swizzled_layout=True, "
+               "SymInt? padded_n=None) -> (Tensor, Tensor)")
+_OUT = ("(Tensor input, Tensor input_scale, bool is_sf_swizzled_layout=True, *, "
+        "Tensor(a!) output, Tensor(b!) output_scale) -> ()")
+
+_OPS = {
+    "scalesweep_mse_nvfp4_quant": (mse.scalesweep_mse_nvfp4_quant_impl,
+                                   mse.scalesweep_mse_nvfp4_quant_out,
+                                   mse._scalesweep_mse_nvfp4_quant_fake),
+    "scalesweep_mse128_nvfp4_quant": (mse.scalesweep_mse128_nvfp4_quant_impl,
+                                      mse.scalesweep_mse128_nvfp4_quant_out,
+                                      mse._scalesweep_mse_nvfp4_quant_fake),
+    "scalesweep_mse_reference_nvfp4_quant": (
+        mse_ref.scalesweep_mse_nvfp4_quant_impl, mse_ref.scalesweep_mse_nvfp4_quant_out,
+        mse_ref._scalesweep_mse_reference_nvfp4_quant_fake),
+    "rtn_nvfp4_quant": (mse.rtn_nvfp4_quant_impl, mse.rtn_nvfp4_quant_out,
+                        mse._scalesweep_mse_nvfp4_quant_fake),
+}
+
+_libs: dict[str, torch.library.Library] = {}
+
+
+def _alloc(input, swizzled, padded_n):
+    """Outputs in their final dtypes (no aliasing views): codes uint8
+    [m, physical_n/2]; scales float8_e4m3fn [round_up(m,128), round_up(bpc,4)]
+    when swizzled, else [m, bpc]."""
+    n = input.shape[-1]
+    m = input.numel() // n if n else 0
+    pn = padded_n if padded_n is not None else n
+    codes = input.new_empty((m, pn // 2), dtype=torch.uint8)
+    bpc = pn // 16
+    shape = ((m + 127) // 128 * 128, (bpc + 3) // 4 * 4) if swizzled else (m, bpc)
+    return codes, input.new_empty(shape, dtype=torch.float8_e4m3fn)
+
+
+def _register(namespace: str, kind: str) -> None:
+    if namespace in _libs:
+        return
+    lib = torch.library.Library(namespace, kind)
+    for name, (_impl, out, fake) in _OPS.items():
+        lib.define(name + _FUNCTIONAL)
+        lib.define(name + ".out" + _OUT)
+
+        def functional(input, input_scale, is_sf_swizzled_layout=True, padded_n=None, _out=out):
+            codes, scales = _alloc(input, is_sf_swizzled_layout, padded_n)
+            _out(input, input_scale, is_sf_swizzled_layout, output=codes, output_scale=scales)
+            return codes, scales
+
+        def out_variant(input, input_scale, is_sf_swizzled_layout=True, *, output, output_scale,
+                        _out=out):
+            _out(input, input_scale, is_sf_swizzled_layout, output=output,
+                 output_scale=output_scale)
+
+        def fake_functional(input, input_scale, is_sf_swizzled_layout=True, padded_n=None,
+                            _fake=fake):
+            _fake(input, input_scale, is_sf_swizzled_layout, padded_n)  # argument checks
+            return _alloc(input, is_sf_swizzled_layout, padded_n)
+
+        def fake_out(input, input_scale, is_sf_swizzled_layout=True, *, output, output_scale):
+            return None
+
+        lib.impl(name, functional, "CUDA")
+        lib.impl(name + ".out", out_variant, "CUDA")
+        torch.library.register_fake(f"{namespace}::{name}", fake_functional, lib=lib)
+        torch.library.register_fake(f"{namespace}::{name}.out", fake_out, lib=lib)
+    _libs[namespace] = lib
+
+
+def register() -> None:
+    """Define the ops under ``torch.ops.scalesweep_b200`` (idempotent)."""
+    _register(NAMESPACE, "DEF")
+
+
+def register_vllm_aliases() -> None:
+    """Also define them under ``torch.ops.vllm`` (for a vLLM build that expects them)."""
+    _register("vllm", "FRAGMENT")
+
+
+register()
