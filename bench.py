@@ -54,6 +54,11 @@ def parse_args():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile-case", default=None, metavar="MxK",
+                    help="only run the scale-sweep quantizer 4 times on one [M, K] input "
+                         "(the command used for ncu captures) and exit")
+    ap.add_argument("--profile-backend", default="scalesweep_mse",
+                    choices=["scalesweep_mse", "scalesweep_mse_reference", "rtn"])
     return ap.parse_args()
 
 
@@ -451,8 +456,24 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_profile_case(args):
+    import torch
+    from test_speed_scalesweep_b200 import custom, global_scale
+    m, k = (int(v) for v in args.profile_case.lower().split("x"))
+    device = torch.device("cuda", 0)
+    x = make_shard(m, k, 99, device)
+    gsi = global_scale.global_scale_inv_from_max(x, FP8_MAX)
+    for _ in range(4):
+        custom.nvfp4_quant(x, gsi, True, args.profile_backend)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": [m, k], "backend": args.profile_backend}))
+
+
 def main():
     args = parse_args()
+    if args.profile_case:
+        run_profile_case(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

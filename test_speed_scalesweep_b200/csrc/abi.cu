@@ -91,6 +91,7 @@ int quant_out(const char* name, int variant, int mode, const void* input, int in
   p.bpc_in = (uint32_t)bpc_in;
   p.bpc_out = (uint32_t)bpc_out;
   p.bpc_pad = (uint32_t)((bpc_out + 3) / 4 * 4);
+  ssw::make_divider(p.bpc_out, &p.div_magic, &p.div_shift);
   p.swizzled = swizzled ? 1 : 0;
   p.scale_word_stores = (bpc_out % 4 == 0) && aligned(output_scale, 4);
   const bool vec = aligned(input, 32) && aligned(output, 8);

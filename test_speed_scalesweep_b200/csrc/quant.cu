@@ -30,6 +30,11 @@ constexpr int kThreads = 256;  // the shared tables below rely on 256 threads
 constexpr int kLower = -3;       // bench_kernel/scalesweep_mse_nvfp4_utils.py:17
 constexpr int kWindow = 11;      // UPPER_BOUND - LOWER_BOUND + 1 (:17-18, :452-454)
 constexpr int kMaxRaw = 126;     // REF_MAX_SCALE_RAW (:20)
+constexpr int kWindowTab = 128 + kWindow;  // window positions j = code + 3, code in [-3, 134]
+#ifndef SSW_QUANT_MIN_BLOCKS
+#define SSW_QUANT_MIN_BLOCKS 4
+#endif
+constexpr int kMinBlocksPerSm = SSW_QUANT_MIN_BLOCKS;
 
 struct ScaleEntry {
   float inv;  // 1 / s, IEEE (equals the reference's Triton 1.0 / s for every code)
@@ -118,12 +123,56 @@ __device__ __forceinline__ void consider_pair(uint64_t sse, float s2a, float s2b
   consider(mb, rb, best, best_raw);
 }
 
+// Block |x| maximum straight from the 16-bit inputs.  max.xorsign.abs.{bf16,f16}x2
+// keeps the larger magnitude of each lane and ignores NaN operands, like the
+// reference's tl.maximum(tl.abs(a), tl.abs(b)).  Because rounding is
+// monotonic, max_j |RN(x_j * g)| == RN(max_j |x_j| * |g|) for every block
+// whose normalised values hold no NaN; a block holding a NaN has a NaN
+// squared error for every candidate, so its scale does not depend on amax.
+template <int kDType>
+__device__ __forceinline__ float block_absmax_raw(const uint32_t (&w)[8]) {
+  uint32_t a[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if constexpr (kDType == kDTypeBF16)
+      asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(a[j]) : "r"(w[2 * j]), "r"(w[2 * j + 1]));
+    else
+      asm("max.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(a[j]) : "r"(w[2 * j]), "r"(w[2 * j + 1]));
+  }
+  uint32_t b0, b1, c;
+  if constexpr (kDType == kDTypeBF16) {
+    asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(b0) : "r"(a[0]), "r"(a[1]));
+    asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(b1) : "r"(a[2]), "r"(a[3]));
+    asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(c) : "r"(b0), "r"(b1));
+    const float lo = __uint_as_float((c & 0x7FFFu) << 16);
+    const float hi = __uint_as_float(c & 0x7FFF0000u);
+    return fmaxf(lo, hi);
+  } else {
+    asm("max.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(b0) : "r"(a[0]), "r"(a[1]));
+    asm("max.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(b1) : "r"(a[2]), "r"(a[3]));
+    asm("max.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(c) : "r"(b0), "r"(b1));
+    const float lo = __half2float(__ushort_as_half((unsigned short)(c & 0x7FFFu)));
+    const float hi = __half2float(__ushort_as_half((unsigned short)((c >> 16) & 0x7FFFu)));
+    return fmaxf(lo, hi);
+  }
+}
+
+// Unsigned 32-bit division by the per-launch constant bpc_out:
+// q = (umulhi(n, magic) + n) >> shift (Granlund & Montgomery 1994, round-up
+// multiplier; the 33-bit sum is formed in 64 bits).
+__device__ __forceinline__ uint32_t div_bpc(uint32_t n, uint32_t magic, uint32_t shift) {
+  return (uint32_t)(((uint64_t)__umulhi(n, magic) + n) >> shift);
+}
+
 template <int kVariant, int kMode, int kDType, bool kVec>
-__global__ void __launch_bounds__(kThreads) quant_kernel(QuantParams p) {
-  // Per-code table: reciprocal and square of every E4M3 scale (codes 0..127),
-  // and the signed value of every byte (the reference variant compares the
-  // base code's value with amax/6).
+__global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantParams p) {
+  // tab  : reciprocal and square of the E4M3 scale of every code 0..127
+  //        (code 0 -> 1/0 = inf, used when no candidate wins)
+  // tabw : the same for window position j = code + 3 with the code clamped to
+  //        [1, 126], so candidate i of base code b is tabw[b + i]
+  // tab_s: signed value of every byte (the reference variant's base test)
   __shared__ ScaleEntry tab[128];
+  __shared__ ScaleEntry tabw[kWindowTab];
   __shared__ float tab_s[256];
   {
     const uint32_t c = threadIdx.x;  // kThreads == 256
@@ -134,10 +183,17 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(QuantParams p) {
       asm("rcp.rn.f32 %0, %1;" : "=f"(inv) : "f"(mag));
       tab[c] = ScaleEntry{inv, mul_rn(mag, mag)};
     }
+    if (c < kWindowTab) {
+      const float s = e4m3_value((uint32_t)clamp_raw((int)c + kLower));
+      float inv;
+      asm("rcp.rn.f32 %0, %1;" : "=f"(inv) : "f"(s));
+      tabw[c] = ScaleEntry{inv, mul_rn(s, s)};
+    }
   }
   __syncthreads();
 
   const float gsi = __ldg(p.input_scale);
+  const float abs_gsi = fabsf(gsi);
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t warp = ((uint64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
   const uint64_t nwarps = ((uint64_t)gridDim.x * kThreads) >> 5;
@@ -147,11 +203,11 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(QuantParams p) {
     const uint64_t b = first + lane;
     const bool valid = b < p.nblocks;
     const uint32_t bb = (uint32_t)b;
-    const uint32_t row = valid ? bb / bpc_out : 0;
+    const uint32_t row = valid ? div_bpc(bb, p.div_magic, p.div_shift) : 0;
     const uint32_t col = valid ? bb - row * bpc_out : 0;
     const bool has_data = valid && col < bpc_in;
 
-    // ---- load + normalise (bench_kernel/scalesweep_mse_nvfp4_utils.py:232-270)
+    // ---- load (bench_kernel/scalesweep_mse_nvfp4_utils.py:232-270)
     uint32_t w[8];
     if (has_data) {
       const uint16_t* src = p.input + ((uint64_t)row * bpc_in + col) * 16;
@@ -166,6 +222,7 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(QuantParams p) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) w[j] = 0u;
     }
+    // ---- normalise: v = float(x) * gsi
     uint64_t vp[8];
     const uint64_t g2 = pack2(gsi, gsi);
 #pragma unroll
@@ -182,40 +239,45 @@ __global__ void __launch_bounds__(kThreads) quant_kernel(QuantParams p) {
     }
 
     // ---- block amax (:209-229) and base code (:353-354; reference :347-351)
-    float m[8];
+    float amax;
+    if constexpr (kMode == kModeRtn) {
+      float m[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float lo, hi;
-      unpack2(vp[j], lo, hi);
-      m[j] = fmaxf(fabsf(lo), fabsf(hi));
+      for (int j = 0; j < 8; ++j) {
+        float lo, hi;
+        unpack2(vp[j], lo, hi);
+        m[j] = fmaxf(fabsf(lo), fabsf(hi));
+      }
+      amax = fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])),
+                   fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
+    } else {
+      amax = mul_rn(block_absmax_raw<kDType>(w), abs_gsi);
     }
-    const float amax = fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])),
-                             fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
     const float base = mul_rn(amax, (float)(1.0 / 6.0));
-    int base_raw = (int)e4m3_code(base);  // 0..255
+    int base_raw = (int)e4m3_code(base);  // 0..127 for base >= 0 or NaN
     if constexpr (kVariant == kVariantReference) {
       base_raw -= (tab_s[base_raw] > base) ? 1 : 0;
     }
+    base_raw = min(base_raw, 127);
 
     // ---- candidate sweep (:356-382)
     int best_raw = 0;
     if constexpr (kMode == kModeRtn) {
       best_raw = clamp_raw(base_raw);
     } else if constexpr (kMode == kModeWindow) {
+      const ScaleEntry* wt = tabw + base_raw;  // candidate i -> wt[i]
       float best = __uint_as_float(0x7F800000u);
+      int bi = -1;
 #pragma unroll
       for (int i = 0; i + 1 < kWindow; i += 2) {
-        const int ra = clamp_raw(base_raw + kLower + i);
-        const int rb = clamp_raw(base_raw + kLower + i + 1);
-        const ScaleEntry ea = tab[ra], eb = tab[rb];
-        consider_pair(sse_pair<kVariant>(vp, ea.inv, eb.inv), ea.s2, eb.s2, ra, rb, best,
-                      best_raw);
+        const ScaleEntry ea = wt[i], eb = wt[i + 1];
+        consider_pair(sse_pair<kVariant>(vp, ea.inv, eb.inv), ea.s2, eb.s2, i, i + 1, best, bi);
       }
       {
-        const int r = clamp_raw(base_raw + kLower + kWindow - 1);
-        const ScaleEntry e = tab[r];
-        consider(mul_rn(sse_one<kVariant>(vp, e.inv), e.s2), r, best, best_raw);
+        const ScaleEntry e = wt[kWindow - 1];
+        consider(mul_rn(sse_one<kVariant>(vp, e.inv), e.s2), kWindow - 1, best, bi);
       }
+      best_raw = bi < 0 ? 0 : clamp_raw(base_raw + kLower + bi);
     } else {  // full range: every code 1..126 (:360-361)
       float best = __uint_as_float(0x7F800000u);
 #pragma unroll 1
@@ -287,12 +349,19 @@ cudaError_t launch_dtype(const QuantParams& p, int dtype, bool vec, int grid, cu
 
 }  // namespace
 
+void make_divider(uint32_t d, uint32_t* magic, uint32_t* shift) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;  // l = ceil(log2 d)
+  *shift = l;
+  *magic = (uint32_t)((((1ull << l) - d) << 32) / d + 1);
+}
+
 int quant_grid_size(uint64_t nblocks, int device_sms) {
   // 8 warps per CTA, 32 blocks per warp per iteration; cap at 4 resident CTAs
   // per SM and let the grid-stride loop cover the rest.
   const uint64_t per_cta = (uint64_t)kThreads;
   uint64_t need = (nblocks + per_cta - 1) / per_cta;
-  const uint64_t cap = (uint64_t)device_sms * 4;
+  const uint64_t cap = (uint64_t)device_sms * kMinBlocksPerSm * 4;
   if (need > cap) need = cap;
   if (need < 1) need = 1;
   return (int)need;

@@ -20,11 +20,15 @@ struct QuantParams {
   uint32_t bpc_in;            // input blocks per row  (n / 16)
   uint32_t bpc_out;           // output blocks per row (physical_n / 16)
   uint32_t bpc_pad;           // round_up(bpc_out, 4)
+  uint32_t div_magic;         // row = (umulhi(b, div_magic) + b) >> div_shift == b / bpc_out
+  uint32_t div_shift;
   int swizzled;
   int scale_word_stores;      // bpc_out % 4 == 0 and output_scale 4-byte aligned
 };
 
 int quant_grid_size(uint64_t nblocks, int device_sms);
+// Round-up multiplier for unsigned 32-bit division by d >= 1.
+void make_divider(uint32_t d, uint32_t* magic, uint32_t* shift);
 cudaError_t launch_quant(const QuantParams& p, int variant, int mode, int dtype, bool vec,
                          int grid, cudaStream_t stream);
 
