@@ -122,6 +122,29 @@ int ssw_global_scale_inv(const void* input, int input_dtype, int64_t numel, floa
                          float* input_scale_out, float* amax_out, void* workspace,
                          void* stream);
 
+/*
+ * ssw_global_scale_inv without any device memory from the caller.  No
+ * counterpart in the reference: the reference computes the global scale with
+ * torch, which allocates.  This entry point is for callers that own only the
+ * input and output buffers -- a plugin inside an engine that plans all device
+ * memory up front, or code running during a CUDA-graph capture that must not
+ * allocate.  It allocates nothing and needs no workspace; its scratch is a
+ * 32 KiB static __device__ array inside the library (held on every GPU that
+ * loads the library until exit), one partial maximum per 32768-element chunk.
+ * Limits and rules:
+ *   - numel <= ssw_global_scale_inv_noalloc_max_numel() (2^28); larger sizes
+ *     return SSW_ERR_INVALID_ARGUMENT with a message;
+ *   - all calls share the scratch: calls that overlap on the GPU race, so
+ *     order them on one stream;
+ *   - the first call on a device looks up the scratch address for that
+ *     device; make it before any stream capture.
+ * Results equal ssw_global_scale_inv's bit for bit.
+ */
+int64_t ssw_global_scale_inv_noalloc_max_numel(void);
+int ssw_global_scale_inv_noalloc(const void* input, int input_dtype, int64_t numel,
+                                 float fp8_max, float* input_scale_out, float* amax_out,
+                                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

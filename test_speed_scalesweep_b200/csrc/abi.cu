@@ -137,6 +137,11 @@ int amax_common(const char* name, const void* input, int input_dtype, int64_t nu
 
 }  // namespace
 
+namespace ssw {
+// Lets other translation units of the library report through ssw_last_error().
+void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+}  // namespace ssw
+
 extern "C" {
 
 int ssw_abi_version(void) { return SSW_ABI_VERSION; }

@@ -1,0 +1,92 @@
+"""The allocation-free global-scale entry point, checked against the regular one.
+
+``ssw_global_scale_inv_noalloc`` exists for callers that own only their input
+and output buffers and cannot hand the library a device workspace: a plugin in
+an engine that plans all device memory up front, or code running inside a
+CUDA-graph capture that must not allocate.  Its scratch is a static array
+inside the library, shared by every call.  This test calls it through the C
+ABI twice in a row, on different inputs, and requires the same bits as
+``ssw_global_scale_inv`` (which uses a caller workspace) every time.  It runs
+the same whether it is the first test in a fresh process (the first call sets
+the scratch address up for the device) or follows the rest of the suite.
+"""
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def lib(built_library):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from test_speed_scalesweep_b200 import _lib
+    return _lib.lib()
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _with_workspace(lib, x, fp8_max):
+    ws = torch.zeros(2, dtype=torch.int32, device=x.device)
+    scale = torch.empty(1, dtype=torch.float32, device=x.device)
+    amax = torch.empty(1, dtype=torch.float32, device=x.device)
+    st = lib.ssw_global_scale_inv(_p(x), 0 if x.dtype == torch.bfloat16 else 1, x.numel(),
+                                  fp8_max, _p(scale), _p(amax), _p(ws),
+                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == 0, lib.ssw_last_error()
+    return scale, amax
+
+
+def _no_alloc(lib, x, fp8_max):
+    scale = torch.empty(1, dtype=torch.float32, device=x.device)
+    amax = torch.empty(1, dtype=torch.float32, device=x.device)
+    st = lib.ssw_global_scale_inv_noalloc(_p(x), 0 if x.dtype == torch.bfloat16 else 1,
+                                          x.numel(), fp8_max, _p(scale), _p(amax),
+                                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == 0, lib.ssw_last_error()
+    return scale, amax
+
+
+def _bits(t):
+    return t.view(torch.int32).item()
+
+
+CASES = [((128, 4096), torch.bfloat16, 448.0, 0),
+         ((4096, 14336), torch.bfloat16, 256.0, 0),
+         ((333, 80), torch.float16, 448.0, 0),
+         ((1, 16), torch.bfloat16, 448.0, 0),
+         ((1000, 48), torch.bfloat16, 448.0, 1)]  # input starts 2 bytes past an aligned address
+
+
+@pytest.mark.parametrize("shape,dtype,fp8_max,offset", CASES)
+def test_no_alloc_matches_workspace_entry_on_two_calls_in_a_row(lib, shape, dtype, fp8_max,
+                                                                offset):
+    g = torch.Generator(device="cuda").manual_seed(shape[0] * 7 + shape[1])
+    numel = shape[0] * shape[1]
+    buf_a = (torch.randn(numel + offset, generator=g, device="cuda") * 3).to(dtype)
+    buf_b = (torch.randn(numel + offset, generator=g, device="cuda") * 50).to(dtype)
+    a = buf_a[offset:].view(shape)
+    b = buf_b[offset:].view(shape)
+    for x in (a, b):  # two calls in a row on different data share the static scratch
+        s_ref, m_ref = _with_workspace(lib, x, fp8_max)
+        s_got, m_got = _no_alloc(lib, x, fp8_max)
+        torch.cuda.synchronize()
+        assert _bits(s_got) == _bits(s_ref)
+        assert _bits(m_got) == _bits(m_ref)
+        assert m_got.item() == x.abs().max().float().item()
+
+
+def test_no_alloc_rejects_tensors_beyond_its_static_scratch(lib):
+    limit = lib.ssw_global_scale_inv_noalloc_max_numel()
+    assert limit == 1 << 28
+    out = torch.empty(1, dtype=torch.float32, device="cuda")
+    x = torch.empty(16, dtype=torch.bfloat16, device="cuda")
+    # the size check runs before anything is read, so a small buffer is enough
+    st = lib.ssw_global_scale_inv_noalloc(_p(x), 0, limit + 1, 448.0, _p(out), None,
+                                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == 1
+    assert "268435456" in lib.ssw_last_error().decode()
