@@ -189,14 +189,39 @@ def kernel_avg_ms(fn, iters: int, stream, flush=None):
     return sum(a.elapsed_time(b) for a, b in evs) / iters
 
 
-def run_sweep(device, reps: int = 10):
-    """Standalone quantizer at the configs of the shape sweep (L2 flushed per launch)."""
+def graph_avg_ms(fn, reps: int, device) -> float:
+    """Per-launch device time of ``fn`` replayed ``reps`` times from one CUDA graph
+    (no L2 flush between launches: the reference's do_bench_cudagraph method)."""
+    import torch
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream(device).wait_stream(side)
+    torch.cuda.synchronize(device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    torch.cuda.synchronize(device)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b) / reps
+    del g
+    return ms
+
+
+def run_sweep(device, reps: int = 20):
+    """Standalone quantizer at the shape-sweep configs, scale-sweep vs RTN."""
     import torch
     from test_speed_scalesweep_b200 import custom, global_scale
     from test_speed_scalesweep_b200 import scalesweep_mse_nvfp4_utils as mse
-    stream = torch.cuda.current_stream(device)
-    flush_buf = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
-    flush = lambda: flush_buf.fill_(1)  # noqa: E731
     out = {}
     for k in SWEEP_K:
         for m in SWEEP_M:
@@ -207,13 +232,13 @@ def run_sweep(device, reps: int = 10):
             for name, fn in (("scalesweep_mse", mse.scalesweep_mse_nvfp4_quant_out),
                              ("rtn", mse.rtn_nvfp4_quant_out)):
                 call = lambda fn=fn: fn(x, gsi, True, output=codes, output_scale=scales)  # noqa
-                for _ in range(3):
-                    call()
-                ms = kernel_avg_ms(call, reps, stream, flush)
+                ms = graph_avg_ms(call, reps, device)
                 res[name] = {"us": round(ms * 1e3, 3),
                              "GB/s": round(m * k * BYTES_PER_ELEM / (ms * 1e-3) / 1e9, 1)}
             out[f"{m}x{k}"] = res
             del x
+    out["method"] = ("per-launch time from one CUDA graph of 20 launches, no L2 flush "
+                     "(inputs of M>=16384 exceed L2)")
     return out
 
 

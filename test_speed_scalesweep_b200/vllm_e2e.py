@@ -1,0 +1,214 @@
+"""vLLM integration: the scale-sweep quantizer as vLLM's NVFP4 activation
+quantizer, plus the end-to-end Llama-3.1-8B W4A4 throughput benchmark.
+
+The reference runs its quantizers inside an unpublished vLLM fork that takes
+an ``act_quant_backend`` argument (``run_bench_tune.sh:24,31``,
+``benchmark_nvfp4_tokens.py:117-118``).  Stock vLLM has no such argument.  Its
+W4A4 linear layer (``CutlassNvFp4LinearKernel.apply_weights``, vLLM 0.22
+``model_executor/kernels/linear/nvfp4/cutlass.py:45-77``) calls the
+module-local name ``scaled_fp4_quant``.  ``install_act_quant_hook`` rebinds
+that name, the same monkey-patch pattern the reference applies to the same
+module in ``benchmark_nvfp4_tokens.py:191-211``.  The replacement calls this
+package's registered torch op, so it traces under torch.compile (fake
+implementation) and runs inside vLLM's CUDA graphs.
+
+The benchmark mirrors ``benchmark_nvfp4_tokens.py``:
+- synthetic prompts of uniform-random token ids, with ``ignore_eos``;
+- a fixed number of output tokens;
+- output tok/s.
+
+It uses the Llama-3.1-8B architecture with random N(0, 0.02) weights,
+RTN-quantized to NVFP4 in-process, because there is no checkpoint.
+
+    python -m test_speed_scalesweep_b200.vllm_e2e --backend scalesweep_mse \
+        --batch-sizes 1 16 64 256 --input-len 1024 --output-len 256
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import tempfile
+import time
+
+import torch
+
+# Llama-3.1-8B architecture hyper-parameters (public model card values).
+LLAMA31_8B = {
+    "architectures": ["LlamaForCausalLM"],
+    "model_type": "llama",
+    "hidden_size": 4096,
+    "intermediate_size": 14336,
+    "num_hidden_layers": 32,
+    "num_attention_heads": 32,
+    "num_key_value_heads": 8,
+    "head_dim": 128,
+    "vocab_size": 128256,
+    "max_position_embeddings": 131072,
+    "rms_norm_eps": 1e-05,
+    "rope_theta": 500000.0,
+    "rope_scaling": {"factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                     "original_max_position_embeddings": 8192, "rope_type": "llama3"},
+    "hidden_act": "silu",
+    "attention_bias": False,
+    "mlp_bias": False,
+    "tie_word_embeddings": False,
+    "torch_dtype": "bfloat16",
+    "bos_token_id": 128000,
+    "eos_token_id": 128009,
+}
+
+# compressed-tensors NVFP4 W4A4: 16-element float4 groups with per-tensor
+# global scales for weights and activations, lm_head left in bf16
+# (quant_model_nvfp4.py:65-87 produces this scheme with llmcompressor).
+_FP4_ARGS = {"num_bits": 4, "type": "float", "strategy": "tensor_group", "group_size": 16,
+             "symmetric": True, "dynamic": False, "observer": "minmax"}
+NVFP4_QUANT_CONFIG = {
+    "quant_method": "compressed-tensors",
+    "format": "nvfp4-pack-quantized",
+    "quantization_status": "compressed",
+    "ignore": ["lm_head"],
+    "config_groups": {
+        "group_0": {
+            "targets": ["Linear"],
+            "format": "nvfp4-pack-quantized",
+            "weights": dict(_FP4_ARGS),
+            "input_activations": dict(_FP4_ARGS, dynamic="local"),
+        }
+    },
+}
+
+BACKENDS = ("scalesweep_mse", "scalesweep_mse_reference", "rtn", "cutlass")
+_OP_FOR_BACKEND = {"scalesweep_mse": "scalesweep_mse_nvfp4_quant",
+                   "scalesweep_mse_reference": "scalesweep_mse_reference_nvfp4_quant",
+                   "rtn": "rtn_nvfp4_quant"}
+
+
+def write_model_dir(path: str) -> str:
+    """A model directory holding only config.json (weights come from the dummy loader)."""
+    os.makedirs(path, exist_ok=True)
+    cfg = dict(LLAMA31_8B, quantization_config=NVFP4_QUANT_CONFIG)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(cfg, f, indent=1)
+    return path
+
+
+def install_act_quant_hook(backend: str) -> None:
+    """Route vLLM's W4A4 activation quantization through this package's kernels.
+
+    ``backend="cutlass"`` leaves vLLM's own quantizer in place (the baseline).
+    """
+    if backend == "cutlass":
+        return
+    from . import ops  # noqa: F401  (registers torch.ops.scalesweep_b200.*)
+    import vllm.model_executor.kernels.linear.nvfp4.cutlass as cutlass_mod
+
+    op = getattr(torch.ops.scalesweep_b200, _OP_FOR_BACKEND[backend])
+
+    def scaled_fp4_quant(input, input_global_scale, is_sf_swizzled_layout=True,
+                         backend="none", padded_n=None):
+        x = input.reshape(-1, input.shape[-1])
+        if padded_n is not None and padded_n == x.shape[-1]:
+            padded_n = None
+        return op(x, input_global_scale, is_sf_swizzled_layout, padded_n)
+
+    cutlass_mod.scaled_fp4_quant = scaled_fp4_quant
+
+
+def init_random_nvfp4_weights(model: torch.nn.Module, act_amax: float = 16.0,
+                              seed: int = 0) -> int:
+    """Give every W4A4 linear layer seeded N(0, 0.02) weights, RTN-quantized to
+    NVFP4 by this package's RTN kernel, and a static activation global scale
+    ``2688 / act_amax``.  Writes in place, so tensors captured by CUDA graphs
+    stay valid.  Returns the number of layers initialised."""
+    from . import global_scale
+    from .scalesweep_mse_nvfp4_utils import rtn_nvfp4_quant_impl
+
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    act_gsi = 448.0 * 6.0 / act_amax
+    count = 0
+    for mod in model.modules():
+        if not (hasattr(mod, "weight_scale") and hasattr(mod, "alpha")
+                and hasattr(mod, "input_global_scale_inv")):
+            continue
+        n = mod.output_size_per_partition
+        k = mod.input_size_per_partition
+        w = torch.empty(n, k, device="cuda", dtype=torch.float32).normal_(0.0, 0.02,
+                                                                          generator=gen)
+        w = w.to(torch.bfloat16)
+        w_gsi = global_scale.global_scale_inv_from_max(w, 448.0)
+        codes, scales = rtn_nvfp4_quant_impl(w, w_gsi, True)
+        mod.weight.data.zero_()
+        mod.weight.data[:, : k // 2].copy_(codes)
+        sc = mod.weight_scale.data
+        sc.view(torch.uint8).zero_()
+        sc.view(torch.uint8)[: scales.shape[0], : scales.shape[1]].copy_(scales.view(torch.uint8))
+        mod.input_global_scale_inv.data.fill_(act_gsi)
+        mod.alpha.data.copy_((1.0 / (act_gsi * w_gsi)).reshape(mod.alpha.shape))
+        count += 1
+    torch.cuda.synchronize()
+    return count
+
+
+def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 0,
+        gpu_memory_utilization: float = 0.85, enforce_eager: bool = False) -> dict:
+    os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
+    install_act_quant_hook(backend)
+    from vllm import LLM, SamplingParams
+    from vllm.inputs import TokensPrompt
+
+    model_dir = write_model_dir(tempfile.mkdtemp(prefix="llama31_8b_nvfp4_"))
+    max_bs = max(batch_sizes)
+    llm = LLM(model=model_dir, skip_tokenizer_init=True, load_format="dummy",
+              dtype="bfloat16", max_model_len=input_len + output_len + 16,
+              max_num_seqs=max_bs, max_num_batched_tokens=max(8192, input_len),
+              gpu_memory_utilization=gpu_memory_utilization, enforce_eager=enforce_eager,
+              seed=seed)
+    n_layers = llm.apply_model(lambda m: init_random_nvfp4_weights(m, seed=seed))
+    gen = torch.Generator().manual_seed(seed)
+    params = SamplingParams(max_tokens=output_len, ignore_eos=True, temperature=1.0,
+                            detokenize=False, seed=seed)
+    results = {"backend": backend, "input_len": input_len, "output_len": output_len,
+               "quantized_layers": n_layers, "batch": {}}
+    warm = [TokensPrompt(prompt_token_ids=torch.randint(0, 128000, (input_len,),
+                                                        generator=gen).tolist())
+            for _ in range(min(16, max_bs))]
+    llm.generate(warm, params, use_tqdm=False)
+    for bs in batch_sizes:
+        prompts = [TokensPrompt(prompt_token_ids=torch.randint(0, 128000, (input_len,),
+                                                               generator=gen).tolist())
+                   for _ in range(bs)]
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        outs = llm.generate(prompts, params, use_tqdm=False)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        n_out = sum(len(o.outputs[0].token_ids) for o in outs)
+        results["batch"][str(bs)] = {
+            "output_tok_s": round(n_out / dt, 2),
+            "total_tok_s": round((n_out + bs * input_len) / dt, 2),
+            "seconds": round(dt, 3), "output_tokens": n_out}
+    return results
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--backend", choices=BACKENDS, default="scalesweep_mse")
+    ap.add_argument("--batch-sizes", type=int, nargs="+", default=[1, 16, 64, 256])
+    ap.add_argument("--input-len", type=int, default=1024)
+    ap.add_argument("--output-len", type=int, default=256)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--enforce-eager", action="store_true")
+    ap.add_argument("--out", default=None)
+    args = ap.parse_args()
+    res = run(args.backend, args.batch_sizes, args.input_len, args.output_len, args.seed,
+              enforce_eager=args.enforce_eager)
+    line = json.dumps(res)
+    print(line, flush=True)
+    if args.out:
+        with open(args.out, "w") as f:
+            f.write(line + "\n")
+
+
+if __name__ == "__main__":
+    main()
