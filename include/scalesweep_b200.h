@@ -123,6 +123,24 @@ int ssw_global_scale_inv(const void* input, int input_dtype, int64_t numel, floa
                          void* stream);
 
 /*
+ * Block-scaled NVFP4 GEMM on the tcgen05 tensor cores:
+ *   out[m, n] (bf16) = alpha[0] * sum_k (a[m,k] * a_scale[m,k/16]) * (b[n,k] * b_scale[n,k/16])
+ * a: [m, k/2] E2M1 codes, b: [n, k/2] E2M1 codes (both K-major, element 2j in
+ * the low nibble), a_scale / b_scale: E4M3 scales in the CUTLASS 128x4
+ * swizzled layout (as written by the quantizers above, is_sf_swizzled_layout=1),
+ * out: [m, n] bf16 row-major.  Requires k % 256 == 0 and n % 128 == 0
+ * (SSW_ERR_UNSUPPORTED otherwise) and 16-byte aligned pointers.  `status`
+ * (optional, device int) becomes non-zero if a bounded device wait gave up.
+ * Replaces vLLM's cutlass_scaled_fp4_mm, which the W4A4 linear layer calls
+ * after activation quantization (vllm 0.22 model_executor/kernels/linear/
+ * nvfp4/cutlass.py:64-71; the reference's fallback restatement is
+ * benchmark_nvfp4_tokens.py:84-106).
+ */
+int ssw_nvfp4_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
+                   const uint8_t* b_scale, const float* alpha, void* out, int64_t m, int64_t n,
+                   int64_t k, int* status, void* stream);
+
+/*
  * ssw_global_scale_inv without any device memory from the caller.  No
  * counterpart in the reference: the reference computes the global scale with
  * torch, which allocates.  This entry point is for callers that own only the

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include "../../include/scalesweep_b200.h"
+#include "gemm.cuh"
 #include "quant.cuh"
 
 namespace {
@@ -194,6 +195,34 @@ int ssw_rtn_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows
   return quant_out("rtn_nvfp4_quant_out", ssw::kVariantMse, ssw::kModeRtn, input, input_dtype,
                    num_rows, n, physical_n, input_scale, output, output_scale,
                    is_sf_swizzled_layout, stream);
+}
+
+int ssw_nvfp4_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
+                   const uint8_t* b_scale, const float* alpha, void* out, int64_t m, int64_t n,
+                   int64_t k, int* status, void* stream) {
+  g_last_error.clear();
+  if (m < 0 || n <= 0 || k <= 0)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_gemm: bad sizes m=%lld n=%lld k=%lld",
+                (long long)m, (long long)n, (long long)k);
+  if (k % 256)
+    return fail(SSW_ERR_UNSUPPORTED, "nvfp4_gemm: k must be a multiple of 256 (got %lld)",
+                (long long)k);
+  if (n % 128)
+    return fail(SSW_ERR_UNSUPPORTED, "nvfp4_gemm: n must be a multiple of 128 (got %lld)",
+                (long long)n);
+  if (m >= (1ll << 31) || n >= (1ll << 31) || k >= (1ll << 31))
+    return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_gemm: sizes must be below 2^31");
+  if (m == 0) return SSW_OK;
+  if (!a || !b || !a_scale || !b_scale || !alpha || !out)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_gemm: null pointer");
+  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(a_scale, 16) || !aligned(b_scale, 16) ||
+      !aligned(out, 16) || !aligned(alpha, 4))
+    return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_gemm: operands must be 16-byte aligned");
+  ssw::gemm::GemmArgs g{a, b, a_scale, b_scale, alpha, out, m, n, k, status};
+  const char* why = "launch";
+  cudaError_t e = ssw::gemm::launch(g, static_cast<cudaStream_t>(stream), &why);
+  if (e != cudaSuccess) return cuda_fail(e, why);
+  return SSW_OK;
 }
 
 int64_t ssw_absmax_workspace_bytes(void) { return 8; }

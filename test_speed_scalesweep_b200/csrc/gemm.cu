@@ -1,0 +1,349 @@
+// Block-scaled NVFP4 GEMM on the 5th-generation tensor cores (sm_100a):
+//
+//   D[m, n] = alpha * sum_k (A[m,k] * sfA[m, k/16]) * (B[n,k] * sfB[n, k/16])      (bf16 out)
+//
+// A: E2M1 codes [M, K/2] bytes (K-major, element 2j in the low nibble),
+// B: E2M1 codes [N, K/2] bytes, sfA / sfB: E4M3 scales in the CUTLASS 128x4
+// swizzled layout that the quantizer writes, alpha: one device float.  This is
+// the operation vLLM's cutlass_scaled_fp4_mm performs for a W4A4 linear layer
+// (vllm 0.22 model_executor/kernels/linear/nvfp4/cutlass.py:64-71).
+//
+// One CTA computes one 128 x 128 output tile:
+//   warp 0 (one lane)  : producer.  TMA tiled loads of the A and B code tiles
+//                        (128 rows x 128 bytes, 128B swizzle; no multicast)
+//                        and 1-D bulk copies of the four 512-byte scale atoms
+//                        of each operand per 256-wide K block, into a
+//                        4-stage shared-memory ring guarded by mbarriers.
+//   warp 1 (one lane)  : tensor-core issuer.  Copies each stage's scale atoms
+//                        to TMEM (tcgen05.cp 32x128b.warpx4), then issues
+//                        4 x tcgen05.mma kind::mxf4nvf4.block_scale.block16
+//                        (M=128, N=128, K=64) accumulating fp32 in TMEM, and
+//                        releases the stage with tcgen05.commit.
+//   warps 0-3          : epilogue.  tcgen05.ld of the 128 x 128 fp32
+//                        accumulator (one TMEM lane quadrant per warp),
+//                        x alpha, round to bf16, store.
+// Every mbarrier wait is bounded; a wait that gives up records an error code
+// in *status and the CTA still frees its TMEM before returning.
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "gemm.cuh"
+
+namespace ssw {
+namespace gemm {
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kBM = 128, kBN = 128;
+constexpr int kBKBytes = 128;                // 256 fp4 values per row per K block
+constexpr int kStages = 4;
+constexpr int kATile = kBM * kBKBytes;       // 16 KiB
+constexpr int kBTile = kBN * kBKBytes;       // 16 KiB
+constexpr int kSFTile = 4 * 512;             // four 128x4 scale atoms (K block of 256)
+constexpr int kStageBytes = kATile + kBTile + 2 * kSFTile;
+constexpr int kTmemCols = 256;               // 128 accumulator + 16 SFA + 16 SFB, pow2
+constexpr int kColSFA = 128, kColSFB = 144;
+constexpr uint32_t kWaitLimit = 1u << 24;    // bounded spin (each try_wait may suspend briefly)
+
+struct __align__(8) Barriers {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Bounded wait for the mbarrier phase with the given parity; false = gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05): start>>4 [0,14), LBO>>4 [16,30),
+// SBO>>4 [32,46), version 1 [46,48), layout type [61,64).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+constexpr uint32_t kLayoutSW128 = 2, kLayoutNone = 0;
+
+// Instruction descriptor, kind::mxf4nvf4 with E4M3 scales: A/B format E2M1 (1)
+// [7,10) [10,13), K-major A and B, N>>3 [17,23), scale format UE4M3 (0) [23],
+// M>>4 [24,29), dense K=64.
+constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+                            ((uint32_t)(kBM >> 4) << 24);
+
+__device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], "
+      "[%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accum), "r"(sfa_tmem), "r"(sfb_tmem));
+}
+
+__device__ __forceinline__ void copy_sf_to_tmem(uint32_t tmem, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem), "l"(sdesc));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void record_error(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
+                      const __grid_constant__ CUtensorMap map_b, const uint8_t* __restrict__ sfa,
+                      const uint8_t* __restrict__ sfb, const float* __restrict__ alpha_ptr,
+                      __nv_bfloat16* __restrict__ out, int m, int n, int k, int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte aligned stage ring (128B-swizzled tiles need 1024 B alignment)
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kStageBytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y;
+  const int kblocks = k / 256;
+  const uint64_t sf_row_stride = (uint64_t)(k / 16) * 128;  // bytes per 128-row scale slab
+  const uint8_t* sfa_tile = sfa + (uint64_t)m_tile * sf_row_stride;
+  const uint8_t* sfb_tile = sfb + (uint64_t)n_tile * sf_row_stride;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)));
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)));
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&bars->tmem_base)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = bars->tmem_base;
+  bool ok = true;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- producer
+    for (int kb = 0; kb < kblocks && ok; ++kb) {
+      const int s = kb % kStages;
+      const uint32_t round = kb / kStages;
+      if (round > 0 && !mbar_wait(&bars->empty[s], (round - 1) & 1)) {
+        record_error(status, 1);
+        ok = false;
+        break;
+      }
+      uint8_t* st = smem + s * kStageBytes;
+      mbar_expect_tx(&bars->full[s], kStageBytes);
+      tma_load_2d(st, &map_a, &bars->full[s], kb * kBKBytes, m_tile * kBM);
+      tma_load_2d(st + kATile, &map_b, &bars->full[s], kb * kBKBytes, n_tile * kBN);
+      bulk_load(st + kATile + kBTile, sfa_tile + (uint64_t)kb * kSFTile, kSFTile, &bars->full[s]);
+      bulk_load(st + kATile + kBTile + kSFTile, sfb_tile + (uint64_t)kb * kSFTile, kSFTile,
+                &bars->full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- tensor-core issuer
+    for (int kb = 0; kb < kblocks && ok; ++kb) {
+      const int s = kb % kStages;
+      if (!mbar_wait(&bars->full[s], (kb / kStages) & 1)) {
+        record_error(status, 2);
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      uint8_t* st = smem + s * kStageBytes;
+      const uint32_t a_base = smem_u32(st), b_base = smem_u32(st + kATile);
+      const uint32_t sfa_base = smem_u32(st + kATile + kBTile);
+      const uint32_t sfb_base = sfa_base + kSFTile;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        // one 512-byte atom = 32 rows x 16 B; 8-row core matrices 128 B apart
+        copy_sf_to_tmem(tmem + kColSFA + 4 * j, smem_desc(sfa_base + 512 * j, 16, 128, kLayoutNone));
+        copy_sf_to_tmem(tmem + kColSFB + 4 * j, smem_desc(sfb_base + 512 * j, 16, 128, kLayoutNone));
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        // K step j: 64 fp4 values = 32 bytes into each 128-byte swizzled row
+        const uint64_t adesc = smem_desc(a_base + 32 * j, 16, 1024, kLayoutSW128);
+        const uint64_t bdesc = smem_desc(b_base + 32 * j, 16, 1024, kLayoutSW128);
+        mma_nvf4(tmem, adesc, bdesc, tmem + kColSFA + 4 * j, tmem + kColSFB + 4 * j,
+                 (kb | j) != 0);
+      }
+      mma_commit(&bars->empty[s]);
+    }
+    mma_commit(&bars->acc_full);
+  }
+  __syncwarp();
+
+  // ---------------- epilogue: every warp reads its 32 accumulator lanes
+  const bool acc_ok = mbar_wait(&bars->acc_full, 0);
+  if (!acc_ok) record_error(status, 3);
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const float alpha = __ldg(alpha_ptr);
+  const int row = m_tile * kBM + warp * 32 + lane;
+#pragma unroll 1
+  for (int c = 0; c < kBN; c += 32) {
+    uint32_t v[32];
+    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c;
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+          "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
+          "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
+          "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    if (acc_ok && row < m) {
+      uint32_t packed[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float lo = __uint_as_float(v[2 * i]) * alpha;
+        const float hi = __uint_as_float(v[2 * i + 1]) * alpha;
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed[i]) : "f"(hi), "f"(lo));
+      }
+      uint4* dst = reinterpret_cast<uint4*>(out + (uint64_t)row * n + (uint64_t)n_tile * kBN + c);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols));
+  }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+bool make_code_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes,
+                   uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {row_bytes, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)kBKBytes, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+}  // namespace
+
+size_t smem_bytes() { return kStages * kStageBytes + sizeof(Barriers) + 1024; }
+
+cudaError_t launch(const GemmArgs& g, cudaStream_t stream, const char** why) {
+  CUtensorMap map_a, map_b;
+  if (!make_code_map(&map_a, g.a, (uint64_t)g.m, (uint64_t)g.k / 2, kBM) ||
+      !make_code_map(&map_b, g.b, (uint64_t)g.n, (uint64_t)g.k / 2, kBN)) {
+    *why = "cuTensorMapEncodeTiled failed";
+    return cudaErrorInvalidValue;
+  }
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *why = "cudaGetDevice";
+    return e;
+  }
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    e = cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem_bytes());
+    if (e != cudaSuccess) {
+      *why = "cudaFuncSetAttribute";
+      return e;
+    }
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  dim3 grid((unsigned)(g.n / kBN), (unsigned)((g.m + kBM - 1) / kBM));
+  nvfp4_gemm_kernel<<<grid, kThreads, smem_bytes(), stream>>>(
+      map_a, map_b, g.sfa, g.sfb, g.alpha, static_cast<__nv_bfloat16*>(g.out), (int)g.m, (int)g.n,
+      (int)g.k, g.status);
+  return cudaGetLastError();
+}
+
+}  // namespace gemm
+}  // namespace ssw

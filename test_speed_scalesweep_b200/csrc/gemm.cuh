@@ -1,0 +1,27 @@
+// Internal launch interface of the NVFP4 GEMM (not part of the C ABI).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+namespace ssw {
+namespace gemm {
+
+struct GemmArgs {
+  const uint8_t* a;    // [m, k/2] E2M1 codes
+  const uint8_t* b;    // [n, k/2] E2M1 codes
+  const uint8_t* sfa;  // swizzled E4M3 scales of A ([round_up(m,128), k/16])
+  const uint8_t* sfb;  // swizzled E4M3 scales of B ([n, k/16])
+  const float* alpha;  // one device float
+  void* out;           // [m, n] bf16
+  int64_t m, n, k;
+  int* status;         // optional device int: set non-zero if a bounded wait gave up
+};
+
+size_t smem_bytes();
+cudaError_t launch(const GemmArgs& g, cudaStream_t stream, const char** why);
+
+}  // namespace gemm
+}  // namespace ssw

@@ -1,0 +1,51 @@
+"""Block-scaled NVFP4 GEMM (tcgen05, sm_100a) with the signature of vLLM's
+``cutlass_scaled_fp4_mm`` (vllm 0.22 ``_custom_ops.py:741-753``), the consumer
+of the quantizer's codes and swizzled scales in a W4A4 linear layer
+(``model_executor/kernels/linear/nvfp4/cutlass.py:64-71``)."""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+
+def cutlass_scaled_fp4_mm(a: torch.Tensor, b: torch.Tensor, block_scale_a: torch.Tensor,
+                          block_scale_b: torch.Tensor, alpha: torch.Tensor,
+                          out_dtype: torch.dtype = torch.bfloat16,
+                          status: torch.Tensor | None = None) -> torch.Tensor:
+    """``alpha * (A ⊙ sfA) @ (B ⊙ sfB)^T`` in bf16.
+
+    a: uint8 [M, K/2] E2M1 codes; b: uint8 [N, K/2]; block_scale_a/b: E4M3
+    scales in the 128x4-swizzled layout; alpha: float32 device scalar.
+    K must be a multiple of 256 and N a multiple of 128.
+    """
+    if out_dtype != torch.bfloat16:
+        raise ValueError("only bf16 output is implemented")
+    for name, t in (("a", a), ("b", b), ("block_scale_a", block_scale_a),
+                    ("block_scale_b", block_scale_b), ("alpha", alpha)):
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError("a [M, K/2] and b [N, K/2] must share K")
+    m, n, k = a.shape[0], b.shape[0], a.shape[1] * 2
+    kpad = (k // 16 + 3) // 4 * 4
+    if block_scale_a.numel() * block_scale_a.element_size() < (m + 127) // 128 * 128 * kpad:
+        raise ValueError("block_scale_a is smaller than the swizzled layout of A")
+    if block_scale_b.numel() * block_scale_b.element_size() < (n + 127) // 128 * 128 * kpad:
+        raise ValueError("block_scale_b is smaller than the swizzled layout of B")
+    if alpha.dtype != torch.float32:
+        raise ValueError("alpha must be float32")
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+    st_ptr = ctypes.c_void_p(status.data_ptr()) if status is not None else None
+    with torch.cuda.device(a.device):
+        st = _lib.lib().ssw_nvfp4_gemm(
+            ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()),
+            ctypes.c_void_p(block_scale_a.data_ptr()), ctypes.c_void_p(block_scale_b.data_ptr()),
+            ctypes.c_void_p(alpha.data_ptr()), ctypes.c_void_p(out.data_ptr()), m, n, k, st_ptr,
+            ctypes.c_void_p(_lib.stream_handle(a.device)))
+    _lib.check(st)
+    return out

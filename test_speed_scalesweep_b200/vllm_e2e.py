@@ -93,26 +93,49 @@ def write_model_dir(path: str) -> str:
     return path
 
 
-def install_act_quant_hook(backend: str) -> None:
+HOOK_CALLS = {"count": 0}
+
+
+def install_act_quant_hook(backend: str) -> int:
     """Route vLLM's W4A4 activation quantization through this package's kernels.
 
-    ``backend="cutlass"`` leaves vLLM's own quantizer in place (the baseline).
+    Every vLLM module that imported ``scaled_fp4_quant`` by name (the CUTLASS
+    and FlashInfer NVFP4 linear kernels among them) gets the replacement, so
+    the hook holds whichever linear backend vLLM picks.  ``backend="cutlass"``
+    leaves vLLM's own quantizer in place (the baseline).  Returns the number
+    of module-level names rebound.
     """
     if backend == "cutlass":
-        return
-    from . import ops  # noqa: F401  (registers torch.ops.scalesweep_b200.*)
-    import vllm.model_executor.kernels.linear.nvfp4.cutlass as cutlass_mod
+        return 0
+    import importlib
+    import sys
 
+    from . import ops  # noqa: F401  (registers torch.ops.scalesweep_b200.*)
+    import vllm._custom_ops as vllm_ops
+
+    for mod_name in ("vllm.model_executor.kernels.linear.nvfp4.cutlass",
+                     "vllm.model_executor.kernels.linear.nvfp4.flashinfer"):
+        try:
+            importlib.import_module(mod_name)
+        except Exception:  # pragma: no cover - depends on the vLLM build
+            pass
+    original = vllm_ops.scaled_fp4_quant
     op = getattr(torch.ops.scalesweep_b200, _OP_FOR_BACKEND[backend])
 
     def scaled_fp4_quant(input, input_global_scale, is_sf_swizzled_layout=True,
                          backend="none", padded_n=None):
+        HOOK_CALLS["count"] += 1
         x = input.reshape(-1, input.shape[-1])
         if padded_n is not None and padded_n == x.shape[-1]:
             padded_n = None
         return op(x, input_global_scale, is_sf_swizzled_layout, padded_n)
 
-    cutlass_mod.scaled_fp4_quant = scaled_fp4_quant
+    rebound = 0
+    for name, mod in list(sys.modules.items()):
+        if name.startswith("vllm") and getattr(mod, "scaled_fp4_quant", None) is original:
+            setattr(mod, "scaled_fp4_quant", scaled_fp4_quant)
+            rebound += 1
+    return rebound
 
 
 def init_random_nvfp4_weights(model: torch.nn.Module, act_amax: float = 16.0,
@@ -153,7 +176,7 @@ def init_random_nvfp4_weights(model: torch.nn.Module, act_amax: float = 16.0,
 def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 0,
         gpu_memory_utilization: float = 0.85, enforce_eager: bool = False) -> dict:
     os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
-    install_act_quant_hook(backend)
+    rebound = install_act_quant_hook(backend)
     from vllm import LLM, SamplingParams
     from vllm.inputs import TokensPrompt
 
@@ -163,13 +186,23 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
               dtype="bfloat16", max_model_len=input_len + output_len + 16,
               max_num_seqs=max_bs, max_num_batched_tokens=max(8192, input_len),
               gpu_memory_utilization=gpu_memory_utilization, enforce_eager=enforce_eager,
-              seed=seed)
+              seed=seed,
+              # the CUTLASS W4A4 linear kernel for every backend, and no
+              # norm/activation-quant fusion, so the activation quantizer under
+              # test is the one that runs (as in the reference's runs,
+              # run_bench_tune.sh:24,31)
+              kernel_config={"linear_backend": "cutlass"},
+              compilation_config={"pass_config": {"fuse_act_quant": False,
+                                                  "fuse_norm_quant": False}})
     n_layers = llm.apply_model(lambda m: init_random_nvfp4_weights(m, seed=seed))
     gen = torch.Generator().manual_seed(seed)
     params = SamplingParams(max_tokens=output_len, ignore_eos=True, temperature=1.0,
                             detokenize=False, seed=seed)
     results = {"backend": backend, "input_len": input_len, "output_len": output_len,
-               "quantized_layers": n_layers, "batch": {}}
+               "quantized_layers": n_layers, "hook_rebound_names": rebound, "batch": {},
+               "linear_backend": "cutlass", "fusion": "off",
+               "weights": "random N(0, 0.02), RTN-quantized to NVFP4 in-process",
+               "prompts": "uniform-random token ids, ignore_eos"}
     warm = [TokensPrompt(prompt_token_ids=torch.randint(0, 128000, (input_len,),
                                                         generator=gen).tolist())
             for _ in range(min(16, max_bs))]
@@ -188,6 +221,7 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
             "output_tok_s": round(n_out / dt, 2),
             "total_tok_s": round((n_out + bs * input_len) / dt, 2),
             "seconds": round(dt, 3), "output_tokens": n_out}
+    results["hook_calls_during_compile_and_capture"] = HOOK_CALLS["count"]
     return results
 
 

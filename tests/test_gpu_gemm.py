@@ -1,0 +1,67 @@
+"""NVFP4 GEMM (tcgen05) against the CPU dequantize-matmul oracle and, when vLLM's
+compiled ops are present, against vLLM's CUTLASS NVFP4 GEMM.  Bar: relative
+Frobenius error <= 1e-2 (bf16 output rounding alone is ~2e-3)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+@pytest.fixture(scope="module")
+def lib(built_library):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from test_speed_scalesweep_b200 import _lib
+    return _lib.lib()
+
+
+def _quantized(rows, k, seed, std, backend):
+    from test_speed_scalesweep_b200 import custom, global_scale
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = (torch.randn(rows, k, generator=g, device="cuda") * std).to(torch.bfloat16)
+    gsi = global_scale.global_scale_inv_from_max(x, 448.0)
+    codes, scales = custom.nvfp4_quant(x, gsi, True, backend)
+    return x, gsi, codes, scales
+
+
+def _rel_fro(got, ref):
+    got = np.asarray(got, np.float64)
+    return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 128, 256), (16, 256, 512), (200, 384, 1024),
+                                   (1, 128, 4096), (1024, 512, 4096)])
+def test_gemm_matches_dequant_matmul_oracle(lib, m, n, k):
+    from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm
+    _, gsi_a, qa, sa = _quantized(m, k, 1 + m, 1.0, "scalesweep_mse")
+    _, gsi_b, qb, sb = _quantized(n, k, 2 + n, 0.02, "rtn")
+    alpha = (1.0 / (gsi_a * gsi_b)).reshape(1).float()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = cutlass_scaled_fp4_mm(qa, qb, sa, sb, alpha, torch.bfloat16, status=status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    ref = oracle.gemm(qa.cpu().numpy(), sa.view(torch.uint8).cpu().numpy(), qb.cpu().numpy(),
+                      sb.view(torch.uint8).cpu().numpy(), m, n, k, alpha.item())
+    err = _rel_fro(out.float().cpu().numpy(), ref)
+    assert err <= TOL, err
+
+
+@pytest.mark.parametrize("m,n,k", [(16, 6144, 4096), (128, 4096, 4096), (1024, 4096, 14336)])
+def test_gemm_matches_vllm_cutlass_fp4_gemm(lib, m, n, k):
+    vops = pytest.importorskip("vllm._custom_ops")
+    if not hasattr(torch.ops, "_C") or not hasattr(torch.ops._C, "cutlass_scaled_fp4_mm"):
+        pytest.skip("vLLM compiled CUTLASS FP4 GEMM not available")
+    from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm
+    _, gsi_a, qa, sa = _quantized(m, k, 11, 1.0, "scalesweep_mse")
+    _, gsi_b, qb, sb = _quantized(n, k, 12, 0.02, "rtn")
+    alpha = (1.0 / (gsi_a * gsi_b)).reshape(1).float()
+    ours = cutlass_scaled_fp4_mm(qa, qb, sa, sb, alpha, torch.bfloat16)
+    ref = vops.cutlass_scaled_fp4_mm(qa, qb, sa, sb, alpha, torch.bfloat16)
+    torch.cuda.synchronize()
+    err = _rel_fro(ours.float().cpu().numpy(), ref.float().cpu().numpy().astype(np.float64))
+    assert err <= TOL, err
