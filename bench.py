@@ -38,6 +38,10 @@ METRIC = "scalesweep-MSE NVFP4 quant GB/s (algorithmic M*K*2.5625 B)"
 UNIT = "GB/s"
 WORKLOAD = "row-sharded scale-sweep MSE NVFP4 quantization of bf16 [524288, 8192]"
 SWEEP_M = (1, 16, 64, 256, 1024, 4096, 16384)
+# Llama-3.1-8B linear layers (K -> N): qkv, o, gate_up, down
+GEMM_SHAPES = ((4096, 6144), (4096, 4096), (4096, 28672), (14336, 4096))
+GEMM_M = (16, 128, 1024, 8192)
+FP4_DENSE_NOMINAL_TFLOPS = 9000.0
 SWEEP_K = (4096, 8192, 14336)
 ALU_OPS_PER_ELEM = 35  # sweep's FP32 op count per element (roofline definition)
 SM_COUNT = 148
@@ -54,6 +58,7 @@ def parse_args():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--profile-case", default=None, metavar="MxK",
                     help="only run the scale-sweep quantizer 4 times on one [M, K] input "
                          "(the command used for ncu captures) and exit")
@@ -239,6 +244,59 @@ def run_sweep(device, reps: int = 20):
             del x
     out["method"] = ("per-launch time from one CUDA graph of 20 launches, no L2 flush "
                      "(inputs of M>=16384 exceed L2)")
+    return out
+
+
+def run_gemm_sweep(device, reps: int = 20):
+    """Config 3: quantize + tcgen05 NVFP4 GEMM on the Llama-3.1-8B linear shapes.
+
+    Times (one CUDA graph of ``reps`` launches each): our GEMM, vLLM's CUTLASS
+    NVFP4 GEMM on the same operands when vLLM's compiled ops are importable, and
+    scale-sweep quantization of the activations followed by our GEMM."""
+    import torch
+    from test_speed_scalesweep_b200 import custom, global_scale
+    from test_speed_scalesweep_b200 import scalesweep_mse_nvfp4_utils as mse
+    from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm
+    try:
+        import vllm._custom_ops as vops
+        vllm_mm = vops.cutlass_scaled_fp4_mm if hasattr(torch.ops._C, "cutlass_scaled_fp4_mm") \
+            else None
+    except Exception:
+        vllm_mm = None
+    out = {"peak_tflops": FP4_DENSE_NOMINAL_TFLOPS,
+           "peak_source": "nominal dense FP4 (no measured FP4 peak on this pool)",
+           "method": "per-launch time from one CUDA graph of 20 launches"}
+    for k, n in GEMM_SHAPES:
+        g = torch.Generator(device=device).manual_seed(k + n)
+        w = (torch.randn(n, k, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        w_gsi = global_scale.global_scale_inv_from_max(w, FP8_MAX)
+        qb, sb = mse.rtn_nvfp4_quant_impl(w, w_gsi, True)
+        del w
+        for m in GEMM_M:
+            x = make_shard(m, k, 3 + m + k, device)
+            a_gsi = global_scale.global_scale_inv_from_max(x, FP8_MAX)
+            qa, sa = mse.scalesweep_mse_nvfp4_quant_impl(x, a_gsi, True)
+            alpha = (1.0 / (a_gsi * w_gsi)).reshape(1).float()
+            flops = 2.0 * m * n * k
+            res = {}
+            ms = graph_avg_ms(lambda: cutlass_scaled_fp4_mm(qa, qb, sa, sb, alpha), reps, device)
+            res["gemm_us"] = round(ms * 1e3, 2)
+            res["gemm_tflops"] = round(flops / (ms * 1e-3) / 1e12, 1)
+            res["gemm_frac"] = round(res["gemm_tflops"] / FP4_DENSE_NOMINAL_TFLOPS, 4)
+            if vllm_mm is not None:
+                vms = graph_avg_ms(lambda: vllm_mm(qa, qb, sa, sb, alpha, torch.bfloat16), reps,
+                                   device)
+                res["vllm_cutlass_gemm_us"] = round(vms * 1e3, 2)
+                res["vllm_cutlass_gemm_tflops"] = round(flops / (vms * 1e-3) / 1e12, 1)
+
+            def fused():
+                ca, csa = mse.scalesweep_mse_nvfp4_quant_impl(x, a_gsi, True)
+                return cutlass_scaled_fp4_mm(ca, qb, csa, sb, alpha)
+            qms = graph_avg_ms(fused, reps, device)
+            res["quant_plus_gemm_us"] = round(qms * 1e3, 2)
+            out[f"M{m}_K{k}_N{n}"] = res
+            del x, qa, sa
+        del qb, sb
     return out
 
 
@@ -451,11 +509,14 @@ def run_ours(args):
 
     sweep = None
     cpu = None
+    gemm_res = None
     if rank == 0 and world == 1:
         del x
         torch.cuda.empty_cache()
         if not args.no_sweep:
             sweep = run_sweep(device)
+        if not args.no_gemm:
+            gemm_res = run_gemm_sweep(device)
         if not args.no_cpu:
             cpu = cpu_sample_rate(args.rows)
 
@@ -475,6 +536,8 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         if sweep is not None:
             line["sweep"] = sweep
+        if gemm_res is not None:
+            line["gemm"] = gemm_res
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -83,6 +83,23 @@ int ssw_scalesweep_mse_reference_nvfp4_quant_out(const void* input, int input_dt
                                                  int is_sf_swizzled_layout, void* stream);
 
 /*
+ * Importance-weighted "scalesweep" backend (window) and "scalesweep128"
+ * (full range 1..126): same sweep, but every squared error is rounded on its
+ * own and then summed in element order, because the reference multiplies it
+ * by a per-column importance weight first (always 1 from its host code).
+ * Replaces bench_kernel/scalesweep_nvfp4_utils.py:344-368 (and the launcher :305-341)
+ * (scalesweep_nvfp4_quant_out, scalesweep128_nvfp4_quant_out).
+ */
+int ssw_scalesweep_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows,
+                                   int64_t n, int64_t physical_n, const float* input_scale,
+                                   uint8_t* output, uint8_t* output_scale,
+                                   int is_sf_swizzled_layout, void* stream);
+int ssw_scalesweep128_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows,
+                                      int64_t n, int64_t physical_n, const float* input_scale,
+                                      uint8_t* output, uint8_t* output_scale,
+                                      int is_sf_swizzled_layout, void* stream);
+
+/*
  * Plain round-to-nearest NVFP4 comparator: scale code = clamp(e4m3(amax/6),1,126),
  * codes = e2m1(v / scale), same layouts.  Stands in for vLLM's
  * scaled_fp4_quant.out that bench_kernel/custom.py:24-31 dispatches "cutlass"/"vllm" to.

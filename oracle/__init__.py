@@ -21,7 +21,7 @@ import numpy as np
 
 from . import build as _build
 
-_VARIANTS = {"mse": 0, "reference": 1}
+_VARIANTS = {"mse": 0, "reference": 1, "weighted": 2}
 _MODES = {"window": 0, "full_range": 1, "rtn": 2}
 _DTYPES = {"bf16": 0, "f16": 1}
 SENTINEL = 0xA5

@@ -18,6 +18,9 @@
  *       swizzle                    :18-41
  *   global scale                   bench_kernel/test_kernel_latency.py:65-75
  *       ((fp8_max*6) / amax is torch's Tensor.__rdiv__ = reciprocal(amax) * scalar)
+ *   weighted "scalesweep"          bench_kernel/scalesweep_nvfp4_utils.py:184-302
+ *       (+ "scalesweep128")        rounded squares accumulated with the importance
+ *                                  weights the host passes (all ones, :314)
  *   RTN comparator                 single candidate at the window's base code
  *
  * Hardware semantics the reference's inline PTX and Triton casts rely on,
@@ -40,7 +43,7 @@
 #include <omp.h>
 #endif
 
-enum { ORC_MSE = 0, ORC_REFERENCE = 1 };
+enum { ORC_MSE = 0, ORC_REFERENCE = 1, ORC_WEIGHTED = 2 };
 enum { ORC_WINDOW = 0, ORC_FULL_RANGE = 1, ORC_RTN = 2 };
 enum { ORC_BF16 = 0, ORC_F16 = 1 };
 
@@ -157,6 +160,29 @@ static float block_sse_tree(const float* v, float inv) {
   return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
 }
 
+static float block_sse_weighted(const float* v, float inv) {
+  /* bench_kernel/scalesweep_nvfp4_utils.py:40-149: squares rounded on their
+   * own, times the importance weight (the host always passes ones, :314),
+   * then accumulated: first pair d0^2*w0 + d1^2*w1 via fma, later pairs
+   * fma(d0^2, w0, acc) then fma(d1^2, w1, .) */
+  const float w = 1.0f;
+  float acc = 0.0f;
+  for (int j = 0; j < 16; j += 2) {
+    float x0 = v[j] * inv, x1 = v[j + 1] * inv;
+    float d0 = e2m1_decode(e2m1_encode(x0)) - x0;
+    float d1 = e2m1_decode(e2m1_encode(x1)) - x1;
+    float s0 = d0 * d0, s1 = d1 * d1;
+    if (j == 0) {
+      s0 = s0 * w;
+      acc = fmaf(s1, w, s0);
+    } else {
+      s0 = fmaf(s0, w, acc);
+      acc = fmaf(s1, w, s0);
+    }
+  }
+  return acc;
+}
+
 static uint8_t clamp_raw(int r) {
   return (uint8_t)(r < 1 ? 1 : (r > MAX_SCALE_RAW ? MAX_SCALE_RAW : r));
 }
@@ -194,7 +220,9 @@ static uint8_t quant_block(const float* v, int variant, int mode, uint8_t* code_
                                            : clamp_raw(base_raw + LOWER_BOUND + i);
       float s = e4m3_decode(raw);
       float inv = 1.0f / s;
-      float sse = variant == ORC_REFERENCE ? block_sse_tree(v, inv) : block_sse_chain(v, inv);
+      float sse = variant == ORC_REFERENCE ? block_sse_tree(v, inv)
+                  : variant == ORC_WEIGHTED  ? block_sse_weighted(v, inv)
+                                             : block_sse_chain(v, inv);
       float mse = sse * (s * s);
       /* strict '<': NaN never wins, ties keep the lowest index (:380-382) */
       if (mse < best) { best = mse; best_raw = raw; }

@@ -26,6 +26,8 @@ _SIGNATURES = {
     "ssw_scalesweep_mse_nvfp4_quant_out": (_int, [_c_p, _int, _i64, _i64, _i64, _c_p, _c_p, _c_p, _int, _c_p]),
     "ssw_scalesweep_mse128_nvfp4_quant_out": (_int, [_c_p, _int, _i64, _i64, _i64, _c_p, _c_p, _c_p, _int, _c_p]),
     "ssw_scalesweep_mse_reference_nvfp4_quant_out": (_int, [_c_p, _int, _i64, _i64, _i64, _c_p, _c_p, _c_p, _int, _c_p]),
+    "ssw_scalesweep_nvfp4_quant_out": (_int, [_c_p, _int, _i64, _i64, _i64, _c_p, _c_p, _c_p, _int, _c_p]),
+    "ssw_scalesweep128_nvfp4_quant_out": (_int, [_c_p, _int, _i64, _i64, _i64, _c_p, _c_p, _c_p, _int, _c_p]),
     "ssw_rtn_nvfp4_quant_out": (_int, [_c_p, _int, _i64, _i64, _i64, _c_p, _c_p, _c_p, _int, _c_p]),
     "ssw_absmax_workspace_bytes": (_i64, []),
     "ssw_absmax": (_int, [_c_p, _int, _i64, _c_p, _c_p, _c_p]),

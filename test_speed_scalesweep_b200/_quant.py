@@ -13,6 +13,8 @@ _ENTRY = {
     "mse128": "ssw_scalesweep_mse128_nvfp4_quant_out",
     "reference": "ssw_scalesweep_mse_reference_nvfp4_quant_out",
     "rtn": "ssw_rtn_nvfp4_quant_out",
+    "weighted": "ssw_scalesweep_nvfp4_quant_out",
+    "weighted128": "ssw_scalesweep128_nvfp4_quant_out",
 }
 
 

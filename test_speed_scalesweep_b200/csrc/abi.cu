@@ -189,6 +189,24 @@ int ssw_scalesweep_mse_reference_nvfp4_quant_out(const void* input, int input_dt
                    output, output_scale, is_sf_swizzled_layout, stream);
 }
 
+int ssw_scalesweep_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows,
+                                   int64_t n, int64_t physical_n, const float* input_scale,
+                                   uint8_t* output, uint8_t* output_scale,
+                                   int is_sf_swizzled_layout, void* stream) {
+  return quant_out("scalesweep_nvfp4_quant_out", ssw::kVariantWeighted, ssw::kModeWindow, input,
+                   input_dtype, num_rows, n, physical_n, input_scale, output, output_scale,
+                   is_sf_swizzled_layout, stream);
+}
+
+int ssw_scalesweep128_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows,
+                                      int64_t n, int64_t physical_n, const float* input_scale,
+                                      uint8_t* output, uint8_t* output_scale,
+                                      int is_sf_swizzled_layout, void* stream) {
+  return quant_out("scalesweep128_nvfp4_quant_out", ssw::kVariantWeighted, ssw::kModeFullRange,
+                   input, input_dtype, num_rows, n, physical_n, input_scale, output, output_scale,
+                   is_sf_swizzled_layout, stream);
+}
+
 int ssw_rtn_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows, int64_t n,
                             int64_t physical_n, const float* input_scale, uint8_t* output,
                             uint8_t* output_scale, int is_sf_swizzled_layout, void* stream) {

@@ -16,6 +16,9 @@
 //   "reference" : s_k = fma(d_{2k+1}, d_{2k+1}, d_{2k}*d_{2k}),
 //                 ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7))
 //                 (bench_kernel/scalesweep_mse_reference_nvfp4_utils.py:91-143)
+//   "weighted"  : acc = d1^2 + d0^2, then acc = d^2 + acc per element, every
+//                 square and sum rounded (importance weights of 1;
+//                 bench_kernel/scalesweep_nvfp4_utils.py:40-149, :314)
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -62,6 +65,25 @@ __device__ __forceinline__ uint64_t sse_pair(const uint64_t (&vp)[8], float inv_
       acc = fma2(d1, d1, acc);
     }
     return acc;
+  } else if constexpr (kVariant == kVariantWeighted) {
+    // Squares rounded on their own, then summed in element order (importance
+    // weights of 1: fma(d^2, 1, acc) == add(d^2, acc)).  Scalar mul.rn /
+    // add.rn on purpose: a packed f32x2 multiply feeding a packed add may be
+    // fused into one FMA, which rounds differently from the reference.
+    float acc_a = 0.0f, acc_b = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float xa0, xa1, xb0, xb1, da0, da1, db0, db1;
+      unpack2(mul2(vp[k], ia), xa0, xa1);
+      unpack2(mul2(vp[k], ib), xb0, xb1);
+      e2m1_delta2(xa0, xa1, da0, da1);
+      e2m1_delta2(xb0, xb1, db0, db1);
+      const float sa0 = mul_rn(da0, da0), sa1 = mul_rn(da1, da1);
+      const float sb0 = mul_rn(db0, db0), sb1 = mul_rn(db1, db1);
+      acc_a = (k == 0) ? add_rn(sa1, sa0) : add_rn(sa1, add_rn(sa0, acc_a));
+      acc_b = (k == 0) ? add_rn(sb1, sb0) : add_rn(sb1, add_rn(sb0, acc_b));
+    }
+    return pack2(acc_a, acc_b);
   } else {
     uint64_t s[8];
 #pragma unroll
@@ -91,6 +113,17 @@ __device__ __forceinline__ float sse_one(const uint64_t (&vp)[8], float inv) {
       e2m1_delta2(x0, x1, d0, d1);
       acc = (k == 0) ? mul_rn(d0, d0) : fma_rn(d0, d0, acc);
       acc = fma_rn(d1, d1, acc);
+    }
+    return acc;
+  } else if constexpr (kVariant == kVariantWeighted) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float x0, x1, d0, d1;
+      unpack2(mul2(vp[k], i2), x0, x1);
+      e2m1_delta2(x0, x1, d0, d1);
+      const float s0 = mul_rn(d0, d0), s1 = mul_rn(d1, d1);
+      acc = (k == 0) ? add_rn(s1, s0) : add_rn(s1, add_rn(s0, acc));
     }
     return acc;
   } else {
@@ -373,6 +406,11 @@ cudaError_t launch_quant(const QuantParams& p, int variant, int mode, int dtype,
     if (mode == kModeWindow) return launch_dtype<kVariantMse, kModeWindow>(p, dtype, vec, grid, stream);
     if (mode == kModeFullRange) return launch_dtype<kVariantMse, kModeFullRange>(p, dtype, vec, grid, stream);
     return launch_dtype<kVariantMse, kModeRtn>(p, dtype, vec, grid, stream);
+  }
+  if (variant == kVariantWeighted) {
+    if (mode == kModeFullRange)
+      return launch_dtype<kVariantWeighted, kModeFullRange>(p, dtype, vec, grid, stream);
+    return launch_dtype<kVariantWeighted, kModeWindow>(p, dtype, vec, grid, stream);
   }
   return launch_dtype<kVariantReference, kModeWindow>(p, dtype, vec, grid, stream);
 }

@@ -7,7 +7,7 @@
 
 namespace ssw {
 
-enum { kVariantMse = 0, kVariantReference = 1 };
+enum { kVariantMse = 0, kVariantReference = 1, kVariantWeighted = 2 };
 enum { kModeWindow = 0, kModeFullRange = 1, kModeRtn = 2 };
 enum { kDTypeBF16 = 0, kDTypeF16 = 1 };
 

@@ -44,13 +44,6 @@ def _vllm_rtn(input, input_global_scale, is_sf_swizzled_layout, padded_n):
                                      backend="cutlass", padded_n=padded_n)
 
 
-def _not_built(name):
-    def impl(*args, **kwargs):
-        raise NotImplementedError(
-            f"backend {name!r} (importance-weighted scale sweep) is not implemented by this package")
-    return impl
-
-
 def nvfp4_quant(input: torch.Tensor, input_global_scale: torch.Tensor,
                 is_sf_swizzled_layout: bool = True, backend: str = "scalesweep_mse",
                 padded_n: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
@@ -70,10 +63,11 @@ def nvfp4_quant(input: torch.Tensor, input_global_scale: torch.Tensor,
 
     from . import scalesweep_mse_nvfp4_utils as mse
     from . import scalesweep_mse_reference_nvfp4_utils as mse_reference
+    from . import scalesweep_nvfp4_utils as sweep
 
     implementations = {
-        "scalesweep": _not_built("scalesweep"),
-        "scalesweep128": _not_built("scalesweep128"),
+        "scalesweep": sweep.scalesweep_nvfp4_quant_impl,
+        "scalesweep128": sweep.scalesweep128_nvfp4_quant_impl,
         "scalesweep_mse": mse.scalesweep_mse_nvfp4_quant_impl,
         "scalesweep_mse_reference": mse_reference.scalesweep_mse_nvfp4_quant_impl,
         "scalesweep_mse128": mse.scalesweep_mse128_nvfp4_quant_impl,

@@ -15,6 +15,7 @@ import torch
 
 from . import scalesweep_mse_nvfp4_utils as mse
 from . import scalesweep_mse_reference_nvfp4_utils as mse_ref
+from . import scalesweep_nvfp4_utils as sweep
 
 NAMESPACE = "scalesweep_b200"
 
@@ -35,6 +36,11 @@ _OPS = {
         mse_ref._scalesweep_mse_reference_nvfp4_quant_fake),
     "rtn_nvfp4_quant": (mse.rtn_nvfp4_quant_impl, mse.rtn_nvfp4_quant_out,
                         mse._scalesweep_mse_nvfp4_quant_fake),
+    "scalesweep_nvfp4_quant": (sweep.scalesweep_nvfp4_quant_impl, sweep.scalesweep_nvfp4_quant_out,
+                               mse._scalesweep_mse_nvfp4_quant_fake),
+    "scalesweep128_nvfp4_quant": (sweep.scalesweep128_nvfp4_quant_impl,
+                                  sweep.scalesweep128_nvfp4_quant_out,
+                                  mse._scalesweep_mse_nvfp4_quant_fake),
 }
 
 _libs: dict[str, torch.library.Library] = {}

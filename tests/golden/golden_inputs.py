@@ -83,13 +83,14 @@ def _edge_rows() -> np.ndarray:
 
 CASES = [
     dict(name="cfg1_slice", m=16, k=4096, seed=1, fp8_max=448.0,
-         variants=["mse_swz", "reference_swz", "mse128_swz", "mse_lin"]),
+         variants=["mse_swz", "reference_swz", "mse128_swz", "mse_lin", "weighted_swz",
+                   "weighted128_swz"]),
     dict(name="conv256", m=7, k=2048, seed=2, fp8_max=256.0,
          variants=["mse_swz", "reference_swz"]),
     dict(name="ragged", m=129, k=80, seed=3, fp8_max=448.0,
          variants=["mse_swz", "reference_swz", "mse_lin", "reference_lin"]),
     dict(name="padded", m=33, k=64, seed=4, fp8_max=448.0, padded_n=96,
-         variants=["mse_swz", "mse_lin", "mse128_swz"]),
+         variants=["mse_swz", "mse_lin", "mse128_swz", "weighted_swz"]),
     dict(name="single_row", m=1, k=512, seed=5, fp8_max=448.0,
          variants=["mse_swz", "reference_swz"]),
     dict(name="one_block", m=5, k=16, seed=6, fp8_max=448.0,
@@ -97,13 +98,14 @@ CASES = [
     dict(name="fp16", m=9, k=256, seed=7, fp8_max=448.0, dtype="f16",
          variants=["mse_swz", "reference_swz"]),
     dict(name="edge", m=8, k=256, gsi=1.0, rows="edge",
-         variants=["mse_swz", "reference_swz", "mse128_swz", "mse_lin"]),
+         variants=["mse_swz", "reference_swz", "mse128_swz", "mse_lin", "weighted_swz",
+                   "weighted128_swz"]),
     dict(name="special", m=2, k=256, gsi=1.0, rows="special",
-         variants=["mse_swz", "reference_swz", "mse128_swz"]),
+         variants=["mse_swz", "reference_swz", "mse128_swz", "weighted_swz"]),
     dict(name="huge_gsi", m=3, k=64, seed=8, gsi=1e30,
          variants=["mse_swz", "reference_swz"]),
-    dict(name="wide", m=48, k=1024, seed=9, fp8_max=448.0, rows="wide",
-         variants=["mse_swz", "reference_swz"]),
+    dict(name="wide", m=48, k=1024, seed=10, fp8_max=448.0, rows="wide",
+         variants=["mse_swz", "reference_swz", "weighted_swz", "weighted_lin"]),
 ]
 
 # Full-size pins (config-1 shape): the golden file stores SHA-256 digests of the

@@ -123,6 +123,22 @@ def _pair_sq_err(x0, x1, acc=None):
     return _fma_f32(d1, d1, d0)
 
 
+def _pair_weighted(x0, x1, w0, w1, acc=None):
+    """scalesweep_nvfp4_utils.py:40-111: d^2 rounded, times weight, fma-accumulated."""
+    q0 = e2m1_decode(e2m1_encode(x0))
+    q1 = e2m1_decode(e2m1_encode(x1))
+    with np.errstate(invalid="ignore", over="ignore"):
+        d0 = (q0 - np.asarray(x0, np.float32)).astype(np.float32)
+        d1 = (q1 - np.asarray(x1, np.float32)).astype(np.float32)
+        d0 = (d0 * d0).astype(np.float32)
+        d1 = (d1 * d1).astype(np.float32)
+        if acc is None:
+            d0 = (d0 * np.asarray(w0, np.float32)).astype(np.float32)
+        else:
+            d0 = _fma_f32(d0, w0, acc)
+    return _fma_f32(d1, w1, d0)
+
+
 def _pack16(xs):
     nib = [e2m1_encode(x).astype(np.uint32) for x in xs]
     words = []
@@ -156,6 +172,12 @@ def install_shims():
     pair_acc = ["cvt.rn.satfinite.e2m1x2.f32 b, $2, $1;", "cvt.rn.f16x2.e2m1x2 h, b;",
                 "sub.rn.f32 d0, q0, $1;", "sub.rn.f32 d1, q1, $2;",
                 "fma.rn.f32 d0, d0, d0, $3;", "fma.rn.f32 $0, d1, d1, d0;"]
+    w_plain = ["cvt.rn.satfinite.e2m1x2.f32 b, $2, $1;", "sub.rn.f32 d0, q0, $1;",
+               "mul.rn.f32 d0, d0, d0;", "mul.rn.f32 d1, d1, d1;", "mul.rn.f32 d0, d0, $3;",
+               "fma.rn.f32 $0, d1, $4, d0;"]
+    w_acc = ["cvt.rn.satfinite.e2m1x2.f32 b, $2, $1;", "sub.rn.f32 d0, q0, $1;",
+             "mul.rn.f32 d0, d0, d0;", "mul.rn.f32 d1, d1, d1;", "fma.rn.f32 d0, d0, $3, $5;",
+             "fma.rn.f32 $0, d1, $4, d0;"]
     pack = ["cvt.rn.satfinite.e2m1x2.f32 b0,  $3,  $2;", "cvt.rn.satfinite.e2m1x2.f32 b7,  $17, $16;",
             "mov.b32 $0, {b0, b1, b2, b3};", "mov.b32 $1, {b4, b5, b6, b7};"]
 
@@ -167,6 +189,14 @@ def install_shims():
             assert constraints == "=r,=r," + ",".join(["f"] * 16) and len(data) == 16
             lo, hi = _pack16([d.astype(np.float32) for d in data])
             return _Call([TensorHandle(lo, tl.uint32), TensorHandle(hi, tl.uint32)])
+        if all(s in text for s in w_acc):
+            assert constraints == "=f,f,f,f,f,f" and len(data) == 5
+            return _Call([TensorHandle(_pair_weighted(data[0], data[1], data[2], data[3], data[4]),
+                                       tl.float32)])
+        if all(s in text for s in w_plain):
+            assert constraints == "=f,f,f,f,f" and len(data) == 4
+            return _Call([TensorHandle(_pair_weighted(data[0], data[1], data[2], data[3]),
+                                       tl.float32)])
         if all(s in text for s in pair_acc):
             assert constraints == "=f,f,f,f" and len(data) == 3
             return _Call([TensorHandle(_pair_sq_err(data[0], data[1], data[2]), tl.float32)])
@@ -216,6 +246,9 @@ def load_reference(ref_root):
         triton.Config({"BLOCKS_PER_PROGRAM": 512}, num_warps=16)]
     mse_ref.scalesweep_quantize_kernel.configs = [
         triton.Config({"BLOCKS_PER_PROGRAM": 512, "NUM_STAGES": 2}, num_warps=16)]
+    import scalesweep_nvfp4_utils as weighted
+    weighted._scalesweep_nvfp4_quant_kernel.configs = [
+        triton.Config({"BLOCKS_PER_PROGRAM": 512}, num_warps=16)]
 
     # Output buffers come from torch.empty; pre-fill them with a sentinel so
     # the bytes the kernel leaves untouched are deterministic in the fixture.
@@ -230,7 +263,8 @@ def load_reference(ref_root):
     import torch
     mse.create_fp4_output_tensors = filled(mse.create_fp4_output_tensors)
     mse_ref.create_fp4_output_tensors = filled(mse_ref.create_fp4_output_tensors)
-    return mse, mse_ref
+    weighted.create_fp4_output_tensors = filled(weighted.create_fp4_output_tensors)
+    return mse, mse_ref, weighted
 
 
 SENTINEL = 0xA5
@@ -240,7 +274,7 @@ def main(ref_root):
     import torch
 
     install_shims()
-    mse, mse_ref = load_reference(ref_root)
+    mse, mse_ref, weighted = load_reference(ref_root)
     out = {}
     for case in golden_inputs.CASES:
         name = case["name"]
@@ -261,6 +295,10 @@ def main(ref_root):
                 codes, scales = mse.scalesweep_mse128_nvfp4_quant_impl(xt, gt, swz, padded_n)
             elif kind == "reference":
                 codes, scales = mse_ref.scalesweep_mse_nvfp4_quant_impl(xt, gt, swz, padded_n)
+            elif kind == "weighted":
+                codes, scales = weighted.scalesweep_nvfp4_quant_impl(xt, gt, swz, padded_n)
+            elif kind == "weighted128":
+                codes, scales = weighted.scalesweep128_nvfp4_quant_impl(xt, gt, swz, padded_n)
             else:
                 raise ValueError(variant)
             out[f"{name}/{variant}/codes"] = codes.numpy().copy()

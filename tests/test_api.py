@@ -62,7 +62,8 @@ def test_ops_registered_with_fake_shapes():
     x = torch.empty(300, 4096, dtype=torch.bfloat16, device="meta")
     s = torch.empty(1, dtype=torch.float32, device="meta")
     for name in ("scalesweep_mse_nvfp4_quant", "scalesweep_mse128_nvfp4_quant",
-                 "scalesweep_mse_reference_nvfp4_quant", "rtn_nvfp4_quant"):
+                 "scalesweep_mse_reference_nvfp4_quant", "rtn_nvfp4_quant",
+                 "scalesweep_nvfp4_quant", "scalesweep128_nvfp4_quant"):
         op = getattr(torch.ops.scalesweep_b200, name)
         c, sc = op(x, s, True)
         assert c.shape == (300, 2048) and sc.shape == (384, 256)

@@ -27,7 +27,9 @@ def lib(built_library):
 ENTRY = {"mse": "ssw_scalesweep_mse_nvfp4_quant_out",
          "mse128": "ssw_scalesweep_mse128_nvfp4_quant_out",
          "reference": "ssw_scalesweep_mse_reference_nvfp4_quant_out",
-         "rtn": "ssw_rtn_nvfp4_quant_out"}
+         "rtn": "ssw_rtn_nvfp4_quant_out",
+         "weighted": "ssw_scalesweep_nvfp4_quant_out",
+         "weighted128": "ssw_scalesweep128_nvfp4_quant_out"}
 
 
 def to_device(bits, dtype="bf16"):
@@ -95,12 +97,12 @@ SWEEP = [(m, k) for k in (4096, 8192, 14336) for m in (1, 16, 64, 256, 1024)]
 
 
 @pytest.mark.parametrize("m,k", SWEEP)
-@pytest.mark.parametrize("kind", ["mse", "reference", "rtn"])
+@pytest.mark.parametrize("kind", ["mse", "reference", "rtn", "weighted"])
 def test_kernel_matches_oracle_config2_shapes(lib, m, k, kind):
     x = gi.outlier_activations(m, k, seed=1000 + m + k)
     gsi = gi.torch_style_gsi(x, 448.0 if kind != "mse" else 256.0)
     codes, scales = c_quant(lib, kind, to_device(x), gsi)
-    var = "reference" if kind == "reference" else "mse"
+    var = kind if kind in ("reference", "weighted") else "mse"
     mode = "rtn" if kind == "rtn" else "window"
     oc, os_ = oracle.quantize(x, gsi, variant=var, mode=mode)
     np.testing.assert_array_equal(codes, oc)
@@ -108,16 +110,18 @@ def test_kernel_matches_oracle_config2_shapes(lib, m, k, kind):
 
 
 @pytest.mark.parametrize("m,k,seed", [(300, 1024, 1), (64, 2048, 2), (1, 64, 3)])
-def test_full_range_mode_matches_oracle(lib, m, k, seed):
+@pytest.mark.parametrize("kind", ["mse128", "weighted128"])
+def test_full_range_mode_matches_oracle(lib, m, k, seed, kind):
     x = gi.wide_range_activations(m, k, seed)
     gsi = gi.torch_style_gsi(x, 448.0)
-    codes, scales = c_quant(lib, "mse128", to_device(x), gsi)
-    oc, os_ = oracle.quantize(x, gsi, mode="full_range")
+    codes, scales = c_quant(lib, kind, to_device(x), gsi)
+    oc, os_ = oracle.quantize(x, gsi, mode="full_range",
+                              variant="weighted" if kind == "weighted128" else "mse")
     np.testing.assert_array_equal(codes, oc)
     np.testing.assert_array_equal(scales, os_)
 
 
-@pytest.mark.parametrize("kind", ["mse", "reference"])
+@pytest.mark.parametrize("kind", ["mse", "reference", "weighted"])
 def test_wide_range_inputs_where_variants_differ(lib, kind):
     x = gi.wide_range_activations(512, 2048, 77)
     gsi = gi.torch_style_gsi(x, 448.0)

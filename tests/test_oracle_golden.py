@@ -12,8 +12,10 @@ import oracle
 
 def _kind(variant):
     kind, layout = variant.rsplit("_", 1)
-    return ("reference" if kind == "reference" else "mse",
-            "full_range" if kind == "mse128" else "window", layout == "swz")
+    var = {"reference": "reference", "weighted": "weighted", "weighted128": "weighted"}.get(kind,
+                                                                                            "mse")
+    mode = "full_range" if kind in ("mse128", "weighted128") else "window"
+    return var, mode, layout == "swz"
 
 
 CASES = [(c["name"], v) for c in gi.CASES for v in c["variants"]]
@@ -53,7 +55,9 @@ def test_oracle_full_config1_checksums(golden, case):
 def test_variants_differ_on_wide_range_golden(golden):
     a = golden["wide/mse_swz/scales"]
     b = golden["wide/reference_swz/scales"]
+    c = golden["wide/weighted_swz/scales"]
     assert np.sum(a != b) > 0
+    assert np.sum(a != c) > 0
 
 
 def test_e2m1_encode_thresholds():
