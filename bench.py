@@ -63,7 +63,11 @@ def parse_args():
                     help="only run the scale-sweep quantizer 4 times on one [M, K] input "
                          "(the command used for ncu captures) and exit")
     ap.add_argument("--profile-backend", default="scalesweep_mse",
-                    choices=["scalesweep_mse", "scalesweep_mse_reference", "rtn"])
+                    choices=["scalesweep_mse", "scalesweep_mse_reference", "rtn", "scalesweep"])
+    ap.add_argument("--profile-gemm", default=None, metavar="MxNxK",
+                    help="only run the NVFP4 GEMM 4 times on one shape and exit (for ncu)")
+    ap.add_argument("--profile-amax", default=None, metavar="MxK",
+                    help="only run the fused amax + global-scale kernel 4 times and exit")
     return ap.parse_args()
 
 
@@ -557,10 +561,47 @@ def run_profile_case(args):
     print(json.dumps({"profile_case": [m, k], "backend": args.profile_backend}))
 
 
+def run_profile_gemm(args):
+    import torch
+    from test_speed_scalesweep_b200 import global_scale
+    from test_speed_scalesweep_b200 import scalesweep_mse_nvfp4_utils as mse
+    from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm
+    m, n, k = (int(v) for v in args.profile_gemm.lower().split("x"))
+    device = torch.device("cuda", 0)
+    x = make_shard(m, k, 5, device)
+    w = make_shard(n, k, 6, device)
+    gx = global_scale.global_scale_inv_from_max(x, FP8_MAX)
+    gw = global_scale.global_scale_inv_from_max(w, FP8_MAX)
+    qa, sa = mse.scalesweep_mse_nvfp4_quant_impl(x, gx, True)
+    qb, sb = mse.rtn_nvfp4_quant_impl(w, gw, True)
+    alpha = (1.0 / (gx * gw)).reshape(1).float()
+    for _ in range(4):
+        cutlass_scaled_fp4_mm(qa, qb, sa, sb, alpha)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_gemm": [m, n, k]}))
+
+
+def run_profile_amax(args):
+    import torch
+    from test_speed_scalesweep_b200 import global_scale
+    m, k = (int(v) for v in args.profile_amax.lower().split("x"))
+    x = make_shard(m, k, 7, torch.device("cuda", 0))
+    for _ in range(4):
+        global_scale.global_scale_inv_from_max(x, FP8_MAX)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_amax": [m, k]}))
+
+
 def main():
     args = parse_args()
     if args.profile_case:
         run_profile_case(args)
+        return
+    if args.profile_gemm:
+        run_profile_gemm(args)
+        return
+    if args.profile_amax:
+        run_profile_amax(args)
         return
     if args.impl == "reference":
         run_reference(args)

@@ -146,16 +146,23 @@ int ssw_global_scale_inv(const void* input, int input_dtype, int64_t numel, floa
  * the low nibble), a_scale / b_scale: E4M3 scales in the CUTLASS 128x4
  * swizzled layout (as written by the quantizers above, is_sf_swizzled_layout=1),
  * out: [m, n] bf16 row-major.  Requires k % 256 == 0 and n % 128 == 0
- * (SSW_ERR_UNSUPPORTED otherwise) and 16-byte aligned pointers.  `status`
- * (optional, device int) becomes non-zero if a bounded device wait gave up.
+ * (SSW_ERR_UNSUPPORTED otherwise) and 16-byte aligned pointers.
+ * When the output has too few 128x128 tiles to fill the GPU, the K loop is
+ * split across CTAs; that needs `workspace` of
+ * ssw_nvfp4_gemm_workspace_bytes(m, n, k) bytes (0 when no split is planned).
+ * With a NULL or smaller workspace the GEMM runs unsplit.  Calls sharing a
+ * workspace must not overlap.  `status` (optional, device int) becomes
+ * non-zero if a bounded device wait gave up.
  * Replaces vLLM's cutlass_scaled_fp4_mm, which the W4A4 linear layer calls
  * after activation quantization (vllm 0.22 model_executor/kernels/linear/
  * nvfp4/cutlass.py:64-71; the reference's fallback restatement is
  * benchmark_nvfp4_tokens.py:84-106).
  */
+int64_t ssw_nvfp4_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k);
 int ssw_nvfp4_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
                    const uint8_t* b_scale, const float* alpha, void* out, int64_t m, int64_t n,
-                   int64_t k, int* status, void* stream);
+                   int64_t k, void* workspace, int64_t workspace_bytes, int* status,
+                   void* stream);
 
 /*
  * ssw_global_scale_inv without any device memory from the caller.  No

@@ -215,9 +215,16 @@ int ssw_rtn_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows
                    is_sf_swizzled_layout, stream);
 }
 
+int64_t ssw_nvfp4_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  int sms = 0;
+  if (m <= 0 || n <= 0 || k <= 0 || n % 128 || k % 256 || device_sms(&sms) != SSW_OK) return 0;
+  return (int64_t)ssw::gemm::workspace_bytes(m, n, k, ssw::gemm::choose_splits(m, n, k, sms));
+}
+
 int ssw_nvfp4_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
                    const uint8_t* b_scale, const float* alpha, void* out, int64_t m, int64_t n,
-                   int64_t k, int* status, void* stream) {
+                   int64_t k, void* workspace, int64_t workspace_bytes, int* status,
+                   void* stream) {
   g_last_error.clear();
   if (m < 0 || n <= 0 || k <= 0)
     return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_gemm: bad sizes m=%lld n=%lld k=%lld",
@@ -234,11 +241,19 @@ int ssw_nvfp4_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
   if (!a || !b || !a_scale || !b_scale || !alpha || !out)
     return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_gemm: null pointer");
   if (!aligned(a, 16) || !aligned(b, 16) || !aligned(a_scale, 16) || !aligned(b_scale, 16) ||
-      !aligned(out, 16) || !aligned(alpha, 4))
+      !aligned(out, 16) || !aligned(alpha, 4) || (workspace && !aligned(workspace, 16)))
     return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_gemm: operands must be 16-byte aligned");
-  ssw::gemm::GemmArgs g{a, b, a_scale, b_scale, alpha, out, m, n, k, status};
+  int sms = 0;
+  int st = device_sms(&sms);
+  if (st != SSW_OK) return st;
+  int splits = ssw::gemm::choose_splits(m, n, k, sms);
+  // without (enough) workspace the GEMM runs unsplit
+  if (splits > 1 &&
+      (!workspace || workspace_bytes < (int64_t)ssw::gemm::workspace_bytes(m, n, k, splits)))
+    splits = 1;
+  ssw::gemm::GemmArgs g{a, b, a_scale, b_scale, alpha, out, m, n, k, status, workspace};
   const char* why = "launch";
-  cudaError_t e = ssw::gemm::launch(g, static_cast<cudaStream_t>(stream), &why);
+  cudaError_t e = ssw::gemm::launch(g, splits, static_cast<cudaStream_t>(stream), &why);
   if (e != cudaSuccess) return cuda_fail(e, why);
   return SSW_OK;
 }

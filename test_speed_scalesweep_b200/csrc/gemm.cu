@@ -13,7 +13,9 @@
 //                        (128 rows x 128 bytes, 128B swizzle; no multicast)
 //                        and 1-D bulk copies of the four 512-byte scale atoms
 //                        of each operand per 256-wide K block, into a
-//                        4-stage shared-memory ring guarded by mbarriers.
+//                        3-stage shared-memory ring guarded by mbarriers.
+//   Two CTAs share an SM (110 KiB shared memory and 256 TMEM columns each), so
+//   one CTA's epilogue overlaps the other's main loop.
 //   warp 1 (one lane)  : tensor-core issuer.  Copies each stage's scale atoms
 //                        to TMEM (tcgen05.cp 32x128b.warpx4), then issues
 //                        4 x tcgen05.mma kind::mxf4nvf4.block_scale.block16
@@ -37,7 +39,7 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int kBM = 128, kBN = 128;
 constexpr int kBKBytes = 128;                // 256 fp4 values per row per K block
-constexpr int kStages = 4;
+constexpr int kStages = 3;                   // 3 x 36 KiB: two CTAs fit one SM
 constexpr int kATile = kBM * kBKBytes;       // 16 KiB
 constexpr int kBTile = kBN * kBKBytes;       // 16 KiB
 constexpr int kSFTile = 4 * 512;             // four 128x4 scale atoms (K block of 256)
@@ -142,11 +144,12 @@ __device__ __forceinline__ void record_error(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                       const __grid_constant__ CUtensorMap map_b, const uint8_t* __restrict__ sfa,
                       const uint8_t* __restrict__ sfb, const float* __restrict__ alpha_ptr,
-                      __nv_bfloat16* __restrict__ out, int m, int n, int k, int* status) {
+                      __nv_bfloat16* __restrict__ out, int m, int n, int k, int* status,
+                      float* __restrict__ partials, uint32_t* __restrict__ tile_tickets) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned stage ring (128B-swizzled tiles need 1024 B alignment)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -155,7 +158,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tile = blockIdx.x, m_tile = blockIdx.y;
-  const int kblocks = k / 256;
+  const int splits = gridDim.z, split = blockIdx.z;
+  const int kblocks_all = k / 256;
+  // this CTA's slice of the K blocks (split-K when gridDim.z > 1)
+  const int kb_begin = (int)(((long long)split * kblocks_all) / splits);
+  const int kb_end = (int)(((long long)(split + 1) * kblocks_all) / splits);
+  const int kblocks = kb_end - kb_begin;
   const uint64_t sf_row_stride = (uint64_t)(k / 16) * 128;  // bytes per 128-row scale slab
   const uint8_t* sfa_tile = sfa + (uint64_t)m_tile * sf_row_stride;
   const uint8_t* sfb_tile = sfb + (uint64_t)n_tile * sf_row_stride;
@@ -194,10 +202,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint8_t* st = smem + s * kStageBytes;
       mbar_expect_tx(&bars->full[s], kStageBytes);
-      tma_load_2d(st, &map_a, &bars->full[s], kb * kBKBytes, m_tile * kBM);
-      tma_load_2d(st + kATile, &map_b, &bars->full[s], kb * kBKBytes, n_tile * kBN);
-      bulk_load(st + kATile + kBTile, sfa_tile + (uint64_t)kb * kSFTile, kSFTile, &bars->full[s]);
-      bulk_load(st + kATile + kBTile + kSFTile, sfb_tile + (uint64_t)kb * kSFTile, kSFTile,
+      const int gkb = kb_begin + kb;  // global K block
+      tma_load_2d(st, &map_a, &bars->full[s], gkb * kBKBytes, m_tile * kBM);
+      tma_load_2d(st + kATile, &map_b, &bars->full[s], gkb * kBKBytes, n_tile * kBN);
+      bulk_load(st + kATile + kBTile, sfa_tile + (uint64_t)gkb * kSFTile, kSFTile,
+                &bars->full[s]);
+      bulk_load(st + kATile + kBTile + kSFTile, sfb_tile + (uint64_t)gkb * kSFTile, kSFTile,
                 &bars->full[s]);
     }
   } else if (warp == 1 && lane == 0) {
@@ -240,6 +250,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;");
   const float alpha = __ldg(alpha_ptr);
   const int row = m_tile * kBM + warp * 32 + lane;
+  const int tile_id = m_tile * gridDim.x + n_tile;
+  const uint64_t tile_elems = (uint64_t)kBM * kBN;
+  // split-K: this CTA's fp32 partial tile, row-major [128][128]
+  float* my_part = splits > 1 ? partials + ((uint64_t)split * gridDim.x * gridDim.y + tile_id) *
+                                               tile_elems
+                              : nullptr;
 #pragma unroll 1
   for (int c = 0; c < kBN; c += 32) {
     uint32_t v[32];
@@ -256,18 +272,64 @@ __global__ void __launch_bounds__(kThreads, 1)
           "=r"(v[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-    if (acc_ok && row < m) {
-      uint32_t packed[16];
+    if (!acc_ok || row >= m) continue;
+    if (splits > 1) {
+      float4* dst = reinterpret_cast<float4*>(my_part + (uint64_t)(warp * 32 + lane) * kBN + c);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float lo = __uint_as_float(v[2 * i]) * alpha;
-        const float hi = __uint_as_float(v[2 * i + 1]) * alpha;
-        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed[i]) : "f"(hi), "f"(lo));
+      for (int q = 0; q < 8; ++q)
+        dst[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                             __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+      continue;
+    }
+    uint32_t packed[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float lo = __uint_as_float(v[2 * i]) * alpha;
+      const float hi = __uint_as_float(v[2 * i + 1]) * alpha;
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed[i]) : "f"(hi), "f"(lo));
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + (uint64_t)row * n + (uint64_t)n_tile * kBN + c);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+  }
+  if (splits > 1) {
+    // The last split to finish this tile sums every split's partial in split
+    // order (deterministic) and writes bf16; nobody waits for anybody.
+    __shared__ bool last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0)
+      last = atomicAdd(&tile_tickets[tile_id], 1u) == (uint32_t)(splits - 1);
+    __syncthreads();
+    if (last && acc_ok) {
+      __threadfence();
+      if (row < m) {
+        const uint64_t split_stride = (uint64_t)gridDim.x * gridDim.y * tile_elems;
+        const float* base = partials + (uint64_t)tile_id * tile_elems +
+                            (uint64_t)(warp * 32 + lane) * kBN;
+#pragma unroll 1
+        for (int c = 0; c < kBN; c += 8) {
+          float acc[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+          for (int sp = 0; sp < splits; ++sp) {
+            const float4* src = reinterpret_cast<const float4*>(base + sp * split_stride + c);
+            const float4 p0 = __ldcg(src), p1 = __ldcg(src + 1);
+            acc[0] += p0.x; acc[1] += p0.y; acc[2] += p0.z; acc[3] += p0.w;
+            acc[4] += p1.x; acc[5] += p1.y; acc[6] += p1.z; acc[7] += p1.w;
+          }
+          uint32_t packed[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
+                : "=r"(packed[i])
+                : "f"(acc[2 * i + 1] * alpha), "f"(acc[2 * i] * alpha));
+          *reinterpret_cast<uint4*>(out + (uint64_t)row * n + (uint64_t)n_tile * kBN + c) =
+              make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        }
       }
-      uint4* dst = reinterpret_cast<uint4*>(out + (uint64_t)row * n + (uint64_t)n_tile * kBN + c);
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      if (threadIdx.x == 0) tile_tickets[tile_id] = 0u;
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
@@ -315,7 +377,24 @@ bool make_code_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t r
 
 size_t smem_bytes() { return kStages * kStageBytes + sizeof(Barriers) + 1024; }
 
-cudaError_t launch(const GemmArgs& g, cudaStream_t stream, const char** why) {
+int choose_splits(int64_t m, int64_t n, int64_t k, int device_sms) {
+  const int64_t tiles = (n / kBN) * ((m + kBM - 1) / kBM);
+  const int64_t kblocks = k / 256;
+  const int64_t target = 2 * (int64_t)device_sms;  // two CTAs per SM
+  if (tiles >= target || kblocks < 4) return 1;
+  int64_t s = (target + tiles - 1) / tiles;
+  if (s > kblocks / 2) s = kblocks / 2;  // keep >= 2 K blocks per split
+  if (s > 16) s = 16;
+  return s < 1 ? 1 : (int)s;
+}
+
+size_t workspace_bytes(int64_t m, int64_t n, int64_t k, int splits) {
+  if (splits <= 1) return 0;
+  const int64_t tiles = (n / kBN) * ((m + kBM - 1) / kBM);
+  return (size_t)splits * tiles * kBM * kBN * sizeof(float) + (size_t)tiles * sizeof(uint32_t);
+}
+
+cudaError_t launch(const GemmArgs& g, int splits, cudaStream_t stream, const char** why) {
   CUtensorMap map_a, map_b;
   if (!make_code_map(&map_a, g.a, (uint64_t)g.m, (uint64_t)g.k / 2, kBM) ||
       !make_code_map(&map_b, g.b, (uint64_t)g.n, (uint64_t)g.k / 2, kBN)) {
@@ -338,10 +417,23 @@ cudaError_t launch(const GemmArgs& g, cudaStream_t stream, const char** why) {
     }
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  dim3 grid((unsigned)(g.n / kBN), (unsigned)((g.m + kBM - 1) / kBM));
+  const unsigned gx = (unsigned)(g.n / kBN), gy = (unsigned)((g.m + kBM - 1) / kBM);
+  float* partials = nullptr;
+  uint32_t* tickets = nullptr;
+  if (splits > 1) {
+    partials = static_cast<float*>(g.workspace);
+    tickets = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(g.workspace) +
+                                          (size_t)splits * gx * gy * kBM * kBN * sizeof(float));
+    e = cudaMemsetAsync(tickets, 0, (size_t)gx * gy * sizeof(uint32_t), stream);
+    if (e != cudaSuccess) {
+      *why = "cudaMemsetAsync";
+      return e;
+    }
+  }
+  dim3 grid(gx, gy, (unsigned)splits);
   nvfp4_gemm_kernel<<<grid, kThreads, smem_bytes(), stream>>>(
       map_a, map_b, g.sfa, g.sfb, g.alpha, static_cast<__nv_bfloat16*>(g.out), (int)g.m, (int)g.n,
-      (int)g.k, g.status);
+      (int)g.k, g.status, partials, tickets);
   return cudaGetLastError();
 }
 

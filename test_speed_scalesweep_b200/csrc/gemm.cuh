@@ -18,10 +18,14 @@ struct GemmArgs {
   void* out;           // [m, n] bf16
   int64_t m, n, k;
   int* status;         // optional device int: set non-zero if a bounded wait gave up
+  void* workspace;     // split-K partials + tile tickets (workspace_bytes(...)), 16B aligned
 };
 
 size_t smem_bytes();
-cudaError_t launch(const GemmArgs& g, cudaStream_t stream, const char** why);
+// Split-K factor for a problem on this many SMs (1 = no split).
+int choose_splits(int64_t m, int64_t n, int64_t k, int device_sms);
+size_t workspace_bytes(int64_t m, int64_t n, int64_t k, int splits);
+cudaError_t launch(const GemmArgs& g, int splits, cudaStream_t stream, const char** why);
 
 }  // namespace gemm
 }  // namespace ssw

@@ -14,12 +14,15 @@ from . import _lib
 def cutlass_scaled_fp4_mm(a: torch.Tensor, b: torch.Tensor, block_scale_a: torch.Tensor,
                           block_scale_b: torch.Tensor, alpha: torch.Tensor,
                           out_dtype: torch.dtype = torch.bfloat16,
-                          status: torch.Tensor | None = None) -> torch.Tensor:
+                          status: torch.Tensor | None = None,
+                          split_k: bool = True) -> torch.Tensor:
     """``alpha * (A ⊙ sfA) @ (B ⊙ sfB)^T`` in bf16.
 
     a: uint8 [M, K/2] E2M1 codes; b: uint8 [N, K/2]; block_scale_a/b: E4M3
     scales in the 128x4-swizzled layout; alpha: float32 device scalar.
-    K must be a multiple of 256 and N a multiple of 128.
+    K must be a multiple of 256 and N a multiple of 128.  When the output has
+    too few tiles to fill the GPU the K loop is split across CTAs (workspace
+    from torch's caching allocator); ``split_k=False`` forces one pass.
     """
     if out_dtype != torch.bfloat16:
         raise ValueError("only bf16 output is implemented")
@@ -41,11 +44,15 @@ def cutlass_scaled_fp4_mm(a: torch.Tensor, b: torch.Tensor, block_scale_a: torch
         raise ValueError("alpha must be float32")
     out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
     st_ptr = ctypes.c_void_p(status.data_ptr()) if status is not None else None
+    h = _lib.lib()
     with torch.cuda.device(a.device):
-        st = _lib.lib().ssw_nvfp4_gemm(
+        ws_bytes = int(h.ssw_nvfp4_gemm_workspace_bytes(m, n, k)) if split_k else 0
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=a.device) if ws_bytes else None
+        st = h.ssw_nvfp4_gemm(
             ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()),
             ctypes.c_void_p(block_scale_a.data_ptr()), ctypes.c_void_p(block_scale_b.data_ptr()),
-            ctypes.c_void_p(alpha.data_ptr()), ctypes.c_void_p(out.data_ptr()), m, n, k, st_ptr,
+            ctypes.c_void_p(alpha.data_ptr()), ctypes.c_void_p(out.data_ptr()), m, n, k,
+            ctypes.c_void_p(ws.data_ptr()) if ws is not None else None, ws_bytes, st_ptr,
             ctypes.c_void_p(_lib.stream_handle(a.device)))
     _lib.check(st)
     return out

@@ -65,3 +65,19 @@ def test_gemm_matches_vllm_cutlass_fp4_gemm(lib, m, n, k):
     torch.cuda.synchronize()
     err = _rel_fro(ours.float().cpu().numpy(), ref.float().cpu().numpy().astype(np.float64))
     assert err <= TOL, err
+
+
+@pytest.mark.parametrize("m,n,k", [(16, 4096, 14336), (1, 128, 4096), (200, 384, 1024)])
+def test_split_k_agrees_with_single_pass(lib, m, n, k):
+    from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm
+    assert lib.ssw_nvfp4_gemm_workspace_bytes(m, n, k) > 0  # these shapes are split
+    _, gsi_a, qa, sa = _quantized(m, k, 21, 1.0, "scalesweep_mse")
+    _, gsi_b, qb, sb = _quantized(n, k, 22, 0.02, "rtn")
+    alpha = (1.0 / (gsi_a * gsi_b)).reshape(1).float()
+    split = cutlass_scaled_fp4_mm(qa, qb, sa, sb, alpha, split_k=True)
+    split2 = cutlass_scaled_fp4_mm(qa, qb, sa, sb, alpha, split_k=True)
+    single = cutlass_scaled_fp4_mm(qa, qb, sa, sb, alpha, split_k=False)
+    torch.cuda.synchronize()
+    assert torch.equal(split, split2)  # the split reduction order is fixed
+    err = _rel_fro(split.float().cpu().numpy(), single.float().cpu().numpy().astype(np.float64))
+    assert err <= TOL, err
