@@ -46,6 +46,7 @@ constexpr int kSFTile = 4 * 512;             // four 128x4 scale atoms (K block 
 constexpr int kStageBytes = kATile + kBTile + 2 * kSFTile;
 constexpr int kTmemCols = 256;               // 128 accumulator + 16 SFA + 16 SFB, pow2
 constexpr int kColSFA = 128, kColSFB = 144;
+constexpr int kMaxSplits = 16;
 constexpr uint32_t kWaitLimit = 1u << 24;    // bounded spin (each try_wait may suspend briefly)
 
 struct __align__(8) Barriers {
@@ -252,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int row = m_tile * kBM + warp * 32 + lane;
   const int tile_id = m_tile * gridDim.x + n_tile;
   const uint64_t tile_elems = (uint64_t)kBM * kBN;
-  // split-K: this CTA's fp32 partial tile, row-major [128][128]
+  // split-K: this CTA's fp32 partial tile, stored as [32 column groups][128 rows] float4
   float* my_part = splits > 1 ? partials + ((uint64_t)split * gridDim.x * gridDim.y + tile_id) *
                                                tile_elems
                               : nullptr;
@@ -274,11 +275,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
     if (!acc_ok || row >= m) continue;
     if (splits > 1) {
-      float4* dst = reinterpret_cast<float4*>(my_part + (uint64_t)(warp * 32 + lane) * kBN + c);
+      // partial layout [column group of 4][row]: lanes (rows) of a warp write
+      // 32 consecutive float4s
+      float4* dst = reinterpret_cast<float4*>(my_part) + (warp * 32 + lane);
 #pragma unroll
       for (int q = 0; q < 8; ++q)
-        dst[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                             __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+        dst[(c / 4 + q) * kBM] =
+            make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                        __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
       continue;
     }
     uint32_t packed[16];
@@ -304,29 +308,60 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     if (last && acc_ok) {
       __threadfence();
-      if (row < m) {
-        const uint64_t split_stride = (uint64_t)gridDim.x * gridDim.y * tile_elems;
-        const float* base = partials + (uint64_t)tile_id * tile_elems +
-                            (uint64_t)(warp * 32 + lane) * kBN;
+      // Coalesced pass over the tile's valid rows: float4 i covers column
+      // group i/valid_rows, row i%valid_rows (partials are stored [group][row]);
+      // every split's value is loaded first, then added in split order.
+      const int valid_rows = min(kBM, m - m_tile * kBM);
+      const int n4 = valid_rows * (kBN / 4);
+      const uint64_t split_stride4 = (uint64_t)gridDim.x * gridDim.y * (tile_elems / 4);
+      const float4* part0 = reinterpret_cast<const float4*>(partials) + (uint64_t)tile_id *
+                                                                            (tile_elems / 4);
+      // four float4 positions per thread per pass: 4 x splits loads in flight
+      constexpr int kUnroll = 4;
+      for (int i0 = threadIdx.x; i0 < n4; i0 += kThreads * kUnroll) {
+        float4 acc[kUnroll];
+        uint64_t off[kUnroll];
+        bool ok4[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int i = i0 + u * kThreads;
+          ok4[u] = i < n4;
+          const int ii = ok4[u] ? i : 0;
+          off[u] = (uint64_t)(ii / valid_rows) * kBM + (ii % valid_rows);
+          acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
 #pragma unroll 1
-        for (int c = 0; c < kBN; c += 8) {
-          float acc[8];
+        for (int sp0 = 0; sp0 < splits; sp0 += 4) {
+          float4 p[4][kUnroll];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-          for (int sp = 0; sp < splits; ++sp) {
-            const float4* src = reinterpret_cast<const float4*>(base + sp * split_stride + c);
-            const float4 p0 = __ldcg(src), p1 = __ldcg(src + 1);
-            acc[0] += p0.x; acc[1] += p0.y; acc[2] += p0.z; acc[3] += p0.w;
-            acc[4] += p1.x; acc[5] += p1.y; acc[6] += p1.z; acc[7] += p1.w;
-          }
-          uint32_t packed[4];
+          for (int q = 0; q < 4; ++q)
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
-                : "=r"(packed[i])
-                : "f"(acc[2 * i + 1] * alpha), "f"(acc[2 * i] * alpha));
-          *reinterpret_cast<uint4*>(out + (uint64_t)row * n + (uint64_t)n_tile * kBN + c) =
-              make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            for (int u = 0; u < kUnroll; ++u)
+              if (sp0 + q < splits && ok4[u])
+                p[q][u] = __ldcg(part0 + (sp0 + q) * split_stride4 + off[u]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u)
+              if (sp0 + q < splits && ok4[u]) {  // split order, fixed
+                acc[u].x += p[q][u].x;
+                acc[u].y += p[q][u].y;
+                acc[u].z += p[q][u].z;
+                acc[u].w += p[q][u].w;
+              }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          if (!ok4[u]) continue;
+          const int i = i0 + u * kThreads;
+          const int r = i % valid_rows, c4 = i / valid_rows;
+          uint32_t lo, hi;
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
+              : "=r"(lo) : "f"(acc[u].y * alpha), "f"(acc[u].x * alpha));
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
+              : "=r"(hi) : "f"(acc[u].w * alpha), "f"(acc[u].z * alpha));
+          *reinterpret_cast<uint2*>(out + (uint64_t)(m_tile * kBM + r) * n +
+                                    (uint64_t)n_tile * kBN + 4 * c4) = make_uint2(lo, hi);
         }
       }
       if (threadIdx.x == 0) tile_tickets[tile_id] = 0u;
@@ -378,13 +413,16 @@ bool make_code_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t r
 size_t smem_bytes() { return kStages * kStageBytes + sizeof(Barriers) + 1024; }
 
 int choose_splits(int64_t m, int64_t n, int64_t k, int device_sms) {
+  // Split K only when the output tiles leave SMs idle and K is long enough
+  // that every split keeps at least 8 K blocks: a split CTA's fixed cost
+  // (prologue, pipeline fill, fp32 partial round trip) outweighs the gain on
+  // short K (measured on B200: K=4096 decode shapes ran slower split).
   const int64_t tiles = (n / kBN) * ((m + kBM - 1) / kBM);
   const int64_t kblocks = k / 256;
-  const int64_t target = 2 * (int64_t)device_sms;  // two CTAs per SM
-  if (tiles >= target || kblocks < 4) return 1;
-  int64_t s = (target + tiles - 1) / tiles;
-  if (s > kblocks / 2) s = kblocks / 2;  // keep >= 2 K blocks per split
-  if (s > 16) s = 16;
+  if (tiles >= device_sms || kblocks < 24) return 1;
+  int64_t s = (device_sms + tiles - 1) / tiles;
+  if (s > kblocks / 8) s = kblocks / 8;
+  if (s > kMaxSplits) s = kMaxSplits;
   return s < 1 ? 1 : (int)s;
 }
 
