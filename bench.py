@@ -88,7 +88,8 @@ def load_traffic_profile():
         with open(path) as f:
             for line in f:
                 if line.startswith("dram_bytes_per_block:"):
-                    return float(line.split(":", 1)[1].split()[0]), path
+                    return (float(line.split(":", 1)[1].split()[0]),
+                            os.path.relpath(path, ROOT))
     except OSError:
         pass
     return None, None
