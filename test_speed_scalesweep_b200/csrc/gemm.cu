@@ -47,12 +47,17 @@ constexpr int kStageBytes = kATile + kBTile + 2 * kSFTile;
 constexpr int kTmemCols = 256;               // 128 accumulator + 16 SFA + 16 SFB, pow2
 constexpr int kColSFA = 128, kColSFB = 144;
 constexpr int kMaxSplits = 16;
+// Split-K reduction: 128 rows x 32 fp32 columns of one split's partial
+// (16 KiB, contiguous in the partial layout) per ring slot.
+constexpr int kRedChunkBytes = kBM * 32 * 4;
+constexpr int kRedSlots = kStages * kStageBytes / kRedChunkBytes;
 constexpr uint32_t kWaitLimit = 1u << 24;    // bounded spin (each try_wait may suspend briefly)
 
 struct __align__(8) Barriers {
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t acc_full;
+  uint64_t red_full[kRedSlots];  // split-K reduction: partial chunk landed in ring slot
   uint32_t tmem_base;
 };
 
@@ -141,6 +146,38 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
       : "memory");
 }
 
+// One warp reads its 32-lane quadrant: lane i gets 32 consecutive fp32 columns.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, "
+      "%10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, "
+      "%26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+        "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
+        "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
+        "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 32 fp32 values x alpha -> 32 bf16 (64 contiguous bytes).
+__device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, const uint32_t (&v)[32],
+                                                 float alpha) {
+  uint32_t packed[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float lo = __uint_as_float(v[2 * i]) * alpha;
+    const float hi = __uint_as_float(v[2 * i + 1]) * alpha;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed[i]) : "f"(hi), "f"(lo));
+  }
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    d[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+}
+
 __device__ __forceinline__ void record_error(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
@@ -175,6 +212,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&bars->empty[s], 1);
     }
     mbar_init(&bars->acc_full, 1);
+    for (int r = 0; r < kRedSlots; ++r) mbar_init(&bars->red_full[r], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)));
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)));
@@ -298,20 +336,28 @@ __global__ void __launch_bounds__(kThreads, 2)
       dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
   }
   if (splits > 1) {
-    // The last split to finish this tile sums every split's partial in split
-    // order (deterministic) and writes bf16; nobody waits for anybody.
+    // The last split to finish this tile adds every split's partial in split
+    // order (deterministic) and writes bf16; nobody waits for another CTA.
+    // Its stage ring is idle now: the other splits' partials come in by bulk
+    // copy, kRedSlots chunks in flight, only the tile's valid rows; this
+    // CTA's own partial is still in TMEM.
     __shared__ bool last;
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0)
+    if (threadIdx.x == 0) {
       last = atomicAdd(&tile_tickets[tile_id], 1u) == (uint32_t)(splits - 1);
+      __threadfence();
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
     __syncthreads();
-    if (last && acc_ok) {
+    const int valid_rows = min(kBM, m - m_tile * kBM);
+    if (last && acc_ok && valid_rows * (kBN / 4) <= 2 * 4 * kThreads) {
+      // Few valid rows (decode): at most two passes of plain loads, every
+      // split's value in flight at once.
       __threadfence();
       // Coalesced pass over the tile's valid rows: float4 i covers column
       // group i/valid_rows, row i%valid_rows (partials are stored [group][row]);
       // every split's value is loaded first, then added in split order.
-      const int valid_rows = min(kBM, m - m_tile * kBM);
       const int n4 = valid_rows * (kBN / 4);
       const uint64_t split_stride4 = (uint64_t)gridDim.x * gridDim.y * (tile_elems / 4);
       const float4* part0 = reinterpret_cast<const float4*>(partials) + (uint64_t)tile_id *
@@ -365,8 +411,75 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       if (threadIdx.x == 0) tile_tickets[tile_id] = 0u;
+    } else if (last && acc_ok) {
+      const int others = splits - 1;
+      const int loads = (kBN / 32) * others;
+      const uint64_t split_stride = (uint64_t)gridDim.x * gridDim.y * tile_elems;
+      const float* tile_part0 = partials + (uint64_t)tile_id * tile_elems;
+      const uint32_t run_bytes = (uint32_t)valid_rows * 16u;
+      // load j: column chunk j / others of the (j % others)-th other split, as
+      // one copy of valid_rows x 16 B per column group of 4
+      auto issue = [&](int j) {
+        const int c = j / others, o = j % others, sp = o < split ? o : o + 1;
+        const int slot = j % kRedSlots;
+        const float* src = tile_part0 + sp * split_stride + (uint64_t)c * (kRedChunkBytes / 4);
+        mbar_expect_tx(&bars->red_full[slot], 8u * run_bytes);
+#pragma unroll 1
+        for (int i = 0; i < 8; ++i)
+          bulk_load(smem + slot * kRedChunkBytes + i * kBM * 16, src + i * kBM * 4, run_bytes,
+                    &bars->red_full[slot]);
+      };
+      if (threadIdx.x == 0)
+        for (int j = 0; j < loads && j < kRedSlots; ++j) issue(j);
+      const int r = warp * 32 + lane;  // row within the tile
+      bool red_ok = true;
+      int j = 0;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+#pragma unroll 1
+        for (int sp = 0; sp < splits; ++sp) {
+          if (sp == split) {
+            uint32_t v[32];
+            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32), v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] += __uint_as_float(v[i]);
+            continue;
+          }
+          const int slot = j % kRedSlots;
+          if (red_ok && mbar_wait(&bars->red_full[slot], (uint32_t)(j / kRedSlots) & 1u)) {
+            // slot layout [column group of 4][row]: lanes read consecutive float4s
+            const float4* src = reinterpret_cast<const float4*>(smem + slot * kRedChunkBytes);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 p4 = src[i * kBM + r];
+              acc[4 * i] += p4.x;
+              acc[4 * i + 1] += p4.y;
+              acc[4 * i + 2] += p4.z;
+              acc[4 * i + 3] += p4.w;
+            }
+          } else if (red_ok) {
+            red_ok = false;
+            record_error(status, 5);
+          }
+          __syncthreads();  // slot fully read before it is refilled
+          if (threadIdx.x == 0 && j + kRedSlots < loads) issue(j + kRedSlots);
+          ++j;
+        }
+        const int grow = m_tile * kBM + r;
+        if (grow < m && red_ok) {
+          uint32_t v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(acc[i]);
+          store_row32_bf16(out + (uint64_t)grow * n + (uint64_t)n_tile * kBN + c * 32, v, alpha);
+        }
+      }
+      if (threadIdx.x == 0) tile_tickets[tile_id] = 0u;
     }
   }
+
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   if (warp == 1) {
