@@ -37,7 +37,8 @@ BYTES_PER_ELEM = 2.5625
 METRIC = "scalesweep-MSE NVFP4 quant GB/s (algorithmic M*K*2.5625 B)"
 UNIT = "GB/s"
 WORKLOAD = "row-sharded scale-sweep MSE NVFP4 quantization of bf16 [524288, 8192]"
-SWEEP_M = (1, 16, 64, 256, 1024, 4096, 16384)
+# config-2 rows, plus 128 and 8192, the other rows the reference publishes latencies for
+SWEEP_M = (1, 16, 64, 128, 256, 1024, 4096, 8192, 16384)
 # Llama-3.1-8B linear layers (K -> N): qkv, o, gate_up, down
 GEMM_SHAPES = ((4096, 6144), (4096, 4096), (4096, 28672), (14336, 4096))
 GEMM_M = (16, 128, 1024, 8192)
@@ -444,7 +445,12 @@ def run_ours(args):
     ms_total = start.elapsed_time(end)
     clocks = sampler.stop()
     t = torch.tensor([ms_total], dtype=torch.float64, device=device)
+    rank_ms = [round(ms_total / args.steps, 4)]
     if world > 1:
+        every = torch.zeros(world, dtype=torch.float64, device=device)
+        every[rank] = ms_total / args.steps
+        dist.all_reduce(every, op=dist.ReduceOp.SUM)
+        rank_ms = [round(v, 4) for v in every.tolist()]
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_step = t.item() / args.steps
     total_bytes = args.rows * k * BYTES_PER_ELEM
@@ -536,6 +542,7 @@ def run_ours(args):
                            "l2": "inputs larger than L2 (no flush needed)",
                            "step": "amax -> (NCCL MAX all-reduce if N>1) -> scale -> quantize"},
                 "gpu_launches": launches_per_step * args.steps,
+                "rank_ms_per_step": rank_ms,
                 "roofline": roofline, "clocks": clocks, "e2e": e2e}
         if cpu is not None:
             line["cpu_baseline"] = cpu
