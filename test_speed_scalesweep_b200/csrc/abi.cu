@@ -100,8 +100,9 @@ int quant_out(const char* name, int variant, int mode, const void* input, int in
   int sms = 0;
   int st = device_sms(&sms);
   if (st != SSW_OK) return st;
-  const int grid = ssw::quant_grid_size(nblocks, sms);
-  cudaError_t e = ssw::launch_quant(p, variant, mode, input_dtype, vec, grid,
+  const int lanes = ssw::quant_lanes_per_block(nblocks, sms, mode, vec);
+  const int grid = ssw::quant_grid_size(nblocks, sms, lanes);
+  cudaError_t e = ssw::launch_quant(p, variant, mode, input_dtype, vec, lanes, grid,
                                     static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, name);
   return SSW_OK;

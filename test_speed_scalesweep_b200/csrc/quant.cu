@@ -197,8 +197,26 @@ __device__ __forceinline__ uint32_t div_bpc(uint32_t n, uint32_t magic, uint32_t
   return (uint32_t)(((uint64_t)__umulhi(n, magic) + n) >> shift);
 }
 
-template <int kVariant, int kMode, int kDType, bool kVec>
+// Lexicographic (mse, index) minimum of two partial sweeps; index -1 = no
+// winner.  Merging the per-lane winners of disjoint candidate subsets this way
+// gives the sequential strict-'<' scan's result: the smallest mse, the lowest
+// index among equal ones, NaN and +inf never winning.
+__device__ __forceinline__ void merge_best(float& best, int& bi, float ob, int oi) {
+  if (oi >= 0 && (bi < 0 || ob < best || (ob == best && oi < bi))) {
+    best = ob;
+    bi = oi;
+  }
+}
+
+// kLanes lanes share one 16-element block when the grid would leave the GPU
+// underfilled (decode-sized inputs): each sweeps the window candidates
+// i = sub, sub + kLanes, ... and the lanes merge their winners.  kLanes = 1 is
+// the throughput configuration: one lane per block, all 11 candidates.
+template <int kVariant, int kMode, int kDType, bool kVec, int kLanes>
 __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantParams p) {
+  static_assert(kLanes == 1 || (kMode == kModeWindow && (kLanes == 2 || kLanes == 4)),
+                "lane sharing applies to the 11-candidate window only");
+  constexpr int kBlocksPerWarp = 32 / kLanes;
   // tab  : reciprocal and square of the E4M3 scale of every code 0..127
   //        (code 0 -> 1/0 = inf, used when no candidate wins)
   // tabw : the same for window position j = code + 3 with the code clamped to
@@ -228,12 +246,14 @@ __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantP
   const float gsi = __ldg(p.input_scale);
   const float abs_gsi = fabsf(gsi);
   const uint32_t lane = threadIdx.x & 31;
+  const uint32_t sub = lane % kLanes;  // this lane's share of the block's candidates
   const uint64_t warp = ((uint64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
   const uint64_t nwarps = ((uint64_t)gridDim.x * kThreads) >> 5;
   const uint32_t bpc_out = p.bpc_out, bpc_in = p.bpc_in;
 
-  for (uint64_t first = warp * 32; first < p.nblocks; first += nwarps * 32) {
-    const uint64_t b = first + lane;
+  for (uint64_t first = warp * kBlocksPerWarp; first < p.nblocks;
+       first += nwarps * kBlocksPerWarp) {
+    const uint64_t b = first + lane / kLanes;
     const bool valid = b < p.nblocks;
     const uint32_t bb = (uint32_t)b;
     const uint32_t row = valid ? div_bpc(bb, p.div_magic, p.div_shift) : 0;
@@ -297,6 +317,32 @@ __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantP
     int best_raw = 0;
     if constexpr (kMode == kModeRtn) {
       best_raw = clamp_raw(base_raw);
+    } else if constexpr (kMode == kModeWindow && kLanes > 1) {
+      const ScaleEntry* wt = tabw + base_raw;  // candidate i -> wt[i]
+      constexpr int kSlots = (kWindow + kLanes - 1) / kLanes;  // 3 (4 lanes) or 6 (2 lanes)
+      float best = __uint_as_float(0x7F800000u);
+      int bi = -1;
+#pragma unroll
+      for (int t = 0; t + 1 < kSlots; t += 2) {
+        // the last lane's final slot may fall past the window: evaluated, never considered
+        const int ia = (int)sub + t * kLanes, ib = (int)sub + (t + 1) * kLanes;
+        const ScaleEntry ea = wt[min(ia, kWindow - 1)], eb = wt[min(ib, kWindow - 1)];
+        float ma, mb;
+        unpack2(mul2(sse_pair<kVariant>(vp, ea.inv, eb.inv), pack2(ea.s2, eb.s2)), ma, mb);
+        if (ia < kWindow) consider(ma, ia, best, bi);
+        if (ib < kWindow) consider(mb, ib, best, bi);
+      }
+      if constexpr (kSlots % 2) {
+        const int i = (int)sub + (kSlots - 1) * kLanes;
+        const ScaleEntry e = wt[min(i, kWindow - 1)];
+        const float mm = mul_rn(sse_one<kVariant>(vp, e.inv), e.s2);
+        if (i < kWindow) consider(mm, i, best, bi);
+      }
+#pragma unroll
+      for (int off = 1; off < kLanes; off <<= 1)
+        merge_best(best, bi, __shfl_xor_sync(0xFFFFFFFFu, best, off),
+                   __shfl_xor_sync(0xFFFFFFFFu, bi, off));
+      best_raw = bi < 0 ? 0 : clamp_raw(base_raw + kLower + bi);
     } else if constexpr (kMode == kModeWindow) {
       const ScaleEntry* wt = tabw + base_raw;  // candidate i -> wt[i]
       float best = __uint_as_float(0x7F800000u);
@@ -329,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantP
     for (int j = 0; j < 8; ++j) unpack2(mul2(vp[j], i2), x[2 * j], x[2 * j + 1]);
     const uint32_t lo_word = e2m1x8(x[0], x[1], x[2], x[3], x[4], x[5], x[6], x[7]);
     const uint32_t hi_word = e2m1x8(x[8], x[9], x[10], x[11], x[12], x[13], x[14], x[15]);
-    if (valid) {
+    if (valid && sub == 0) {
       if constexpr (kVec) {
         st_v2(p.output + b * 8, lo_word, hi_word);
       } else {
@@ -354,30 +400,39 @@ __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantP
       // bpc_out % 4 == 0: lanes 4j..4j+3 hold columns 4c..4c+3 of one row,
       // which are four consecutive bytes in both layouts.
       const uint32_t s0 = (uint32_t)best_raw;
-      const uint32_t s1 = __shfl_down_sync(0xFFFFFFFFu, s0, 1);
-      const uint32_t s2 = __shfl_down_sync(0xFFFFFFFFu, s0, 2);
-      const uint32_t s3 = __shfl_down_sync(0xFFFFFFFFu, s0, 3);
-      if (valid && (lane & 3) == 0)
+      const uint32_t s1 = __shfl_down_sync(0xFFFFFFFFu, s0, kLanes);
+      const uint32_t s2 = __shfl_down_sync(0xFFFFFFFFu, s0, 2 * kLanes);
+      const uint32_t s3 = __shfl_down_sync(0xFFFFFFFFu, s0, 3 * kLanes);
+      if (valid && (lane & (4 * kLanes - 1)) == 0)
         *reinterpret_cast<uint32_t*>(p.output_scale + off) = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
-    } else if (valid) {
+    } else if (valid && sub == 0) {
       p.output_scale[off] = (uint8_t)best_raw;
     }
   }
 }
 
-template <int kVariant, int kMode, int kDType, bool kVec>
+template <int kVariant, int kMode, int kDType, bool kVec, int kLanes>
 cudaError_t launch_one(const QuantParams& p, int grid, cudaStream_t stream) {
-  quant_kernel<kVariant, kMode, kDType, kVec><<<grid, kThreads, 0, stream>>>(p);
+  quant_kernel<kVariant, kMode, kDType, kVec, kLanes><<<grid, kThreads, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
+template <int kVariant, int kMode, int kDType>
+cudaError_t launch_lanes(const QuantParams& p, bool vec, int lanes, int grid, cudaStream_t s) {
+  if constexpr (kMode == kModeWindow) {
+    if (vec && lanes == 4) return launch_one<kVariant, kMode, kDType, true, 4>(p, grid, s);
+    if (vec && lanes == 2) return launch_one<kVariant, kMode, kDType, true, 2>(p, grid, s);
+  }
+  if (lanes != 1) return cudaErrorInvalidValue;
+  return vec ? launch_one<kVariant, kMode, kDType, true, 1>(p, grid, s)
+             : launch_one<kVariant, kMode, kDType, false, 1>(p, grid, s);
+}
+
 template <int kVariant, int kMode>
-cudaError_t launch_dtype(const QuantParams& p, int dtype, bool vec, int grid, cudaStream_t s) {
-  if (dtype == kDTypeBF16)
-    return vec ? launch_one<kVariant, kMode, kDTypeBF16, true>(p, grid, s)
-               : launch_one<kVariant, kMode, kDTypeBF16, false>(p, grid, s);
-  return vec ? launch_one<kVariant, kMode, kDTypeF16, true>(p, grid, s)
-             : launch_one<kVariant, kMode, kDTypeF16, false>(p, grid, s);
+cudaError_t launch_dtype(const QuantParams& p, int dtype, bool vec, int lanes, int grid,
+                         cudaStream_t s) {
+  if (dtype == kDTypeBF16) return launch_lanes<kVariant, kMode, kDTypeBF16>(p, vec, lanes, grid, s);
+  return launch_lanes<kVariant, kMode, kDTypeF16>(p, vec, lanes, grid, s);
 }
 
 }  // namespace
@@ -389,10 +444,23 @@ void make_divider(uint32_t d, uint32_t* magic, uint32_t* shift) {
   *magic = (uint32_t)((((1ull << l) - d) << 32) / d + 1);
 }
 
-int quant_grid_size(uint64_t nblocks, int device_sms) {
-  // 8 warps per CTA, 32 blocks per warp per iteration; cap at 4 resident CTAs
-  // per SM and let the grid-stride loop cover the rest.
-  const uint64_t per_cta = (uint64_t)kThreads;
+int quant_lanes_per_block(uint64_t nblocks, int device_sms, int mode, bool vec) {
+  // Every lane of a shared block repeats the load, normalisation and final
+  // encode, so sharing costs throughput.  It pays only while the input is so
+  // small that the lanes still fit in one CTA per SM: the GPU is mostly idle
+  // and the shorter per-lane sweep is pure latency gain (measured on B200:
+  // M=16, K=4096 went from 2.98 to 2.54 us; M=128 got slower when shared).
+  if (mode != kModeWindow || !vec) return 1;
+  const uint64_t one_cta_per_sm = (uint64_t)device_sms * kThreads;
+  if (nblocks * 4 <= one_cta_per_sm) return 4;
+  if (nblocks * 2 <= one_cta_per_sm) return 2;
+  return 1;
+}
+
+int quant_grid_size(uint64_t nblocks, int device_sms, int lanes) {
+  // 8 warps per CTA, 32 / lanes blocks per warp per iteration; cap at 4
+  // resident CTAs per SM and let the grid-stride loop cover the rest.
+  const uint64_t per_cta = (uint64_t)(kThreads / lanes);
   uint64_t need = (nblocks + per_cta - 1) / per_cta;
   const uint64_t cap = (uint64_t)device_sms * kMinBlocksPerSm * 4;
   if (need > cap) need = cap;
@@ -401,18 +469,20 @@ int quant_grid_size(uint64_t nblocks, int device_sms) {
 }
 
 cudaError_t launch_quant(const QuantParams& p, int variant, int mode, int dtype, bool vec,
-                         int grid, cudaStream_t stream) {
+                         int lanes, int grid, cudaStream_t stream) {
   if (variant == kVariantMse) {
-    if (mode == kModeWindow) return launch_dtype<kVariantMse, kModeWindow>(p, dtype, vec, grid, stream);
-    if (mode == kModeFullRange) return launch_dtype<kVariantMse, kModeFullRange>(p, dtype, vec, grid, stream);
-    return launch_dtype<kVariantMse, kModeRtn>(p, dtype, vec, grid, stream);
+    if (mode == kModeWindow)
+      return launch_dtype<kVariantMse, kModeWindow>(p, dtype, vec, lanes, grid, stream);
+    if (mode == kModeFullRange)
+      return launch_dtype<kVariantMse, kModeFullRange>(p, dtype, vec, lanes, grid, stream);
+    return launch_dtype<kVariantMse, kModeRtn>(p, dtype, vec, lanes, grid, stream);
   }
   if (variant == kVariantWeighted) {
     if (mode == kModeFullRange)
-      return launch_dtype<kVariantWeighted, kModeFullRange>(p, dtype, vec, grid, stream);
-    return launch_dtype<kVariantWeighted, kModeWindow>(p, dtype, vec, grid, stream);
+      return launch_dtype<kVariantWeighted, kModeFullRange>(p, dtype, vec, lanes, grid, stream);
+    return launch_dtype<kVariantWeighted, kModeWindow>(p, dtype, vec, lanes, grid, stream);
   }
-  return launch_dtype<kVariantReference, kModeWindow>(p, dtype, vec, grid, stream);
+  return launch_dtype<kVariantReference, kModeWindow>(p, dtype, vec, lanes, grid, stream);
 }
 
 }  // namespace ssw

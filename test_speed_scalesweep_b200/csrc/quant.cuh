@@ -26,11 +26,14 @@ struct QuantParams {
   int scale_word_stores;      // bpc_out % 4 == 0 and output_scale 4-byte aligned
 };
 
-int quant_grid_size(uint64_t nblocks, int device_sms);
+// Lanes sharing one block (1, 2 or 4): more than 1 only for the 11-candidate
+// window with vector loads, when nblocks x lanes fits one wave.
+int quant_lanes_per_block(uint64_t nblocks, int device_sms, int mode, bool vec);
+int quant_grid_size(uint64_t nblocks, int device_sms, int lanes);
 // Round-up multiplier for unsigned 32-bit division by d >= 1.
 void make_divider(uint32_t d, uint32_t* magic, uint32_t* shift);
 cudaError_t launch_quant(const QuantParams& p, int variant, int mode, int dtype, bool vec,
-                         int grid, cudaStream_t stream);
+                         int lanes, int grid, cudaStream_t stream);
 
 // amax / global scale
 struct AmaxParams {
