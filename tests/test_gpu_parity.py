@@ -109,6 +109,33 @@ def test_kernel_matches_oracle_config2_shapes(lib, m, k, kind):
     np.testing.assert_array_equal(scales, os_)
 
 
+def _lane_sharing_shapes():
+    """(m, k) pairs whose block count sits on each side of the 4-lane and 2-lane
+    thresholds (blocks x lanes <= SMs x 256 threads), with k = 16 x 37 so rows
+    end mid-scale-word (byte scale stores)."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count if \
+        torch.cuda.is_available() else 148
+    bpc = 37
+    limit4, limit2 = sms * 256 // 4, sms * 256 // 2
+    return [(limit4 // bpc, 16 * bpc), (limit4 // bpc + 1, 16 * bpc),
+            (limit2 // bpc, 16 * bpc), (limit2 // bpc + 1, 16 * bpc), (3, 4096)]
+
+
+@pytest.mark.parametrize("m,k", _lane_sharing_shapes())
+@pytest.mark.parametrize("kind", ["mse", "reference", "weighted"])
+@pytest.mark.parametrize("swz", [True, False])
+def test_lane_shared_blocks_match_oracle(lib, m, k, kind, swz):
+    # decode-sized inputs give each block 2 or 4 lanes that sweep disjoint
+    # candidate subsets; wide-range values make exact ties and variant
+    # differences likely
+    x = gi.wide_range_activations(m, k, m + k)
+    gsi = gi.torch_style_gsi(x, 448.0)
+    codes, scales = c_quant(lib, kind, to_device(x), gsi, swizzled=swz)
+    oc, os_ = oracle.quantize(x, gsi, variant=kind, swizzled=swz)
+    np.testing.assert_array_equal(codes, oc)
+    np.testing.assert_array_equal(scales, os_)
+
+
 @pytest.mark.parametrize("m,k,seed", [(300, 1024, 1), (64, 2048, 2), (1, 64, 3)])
 @pytest.mark.parametrize("kind", ["mse128", "weighted128"])
 def test_full_range_mode_matches_oracle(lib, m, k, seed, kind):
