@@ -433,6 +433,11 @@ def run_ours(args):
     sampler = ClockSampler(bus)
     sampler.start()
     time.sleep(0.3)
+    # Ranks leave the sampler start-up at different times; line them up right
+    # before the first timed step, or an early rank's window would include
+    # waiting for the others in its first all-reduce.
+    barrier()
+    torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record(stream)
