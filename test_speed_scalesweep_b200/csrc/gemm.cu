@@ -87,7 +87,6 @@ constexpr uint32_t kWaitLimit = 1u << 24;    // bounded spin (each try_wait may 
 struct __align__(8) Barriers {
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
-  uint64_t sf_ready[kMaxStages];  // the stage's scale factors are in TMEM
   uint64_t acc_full;
   uint64_t red_full[kMaxRedSlots];  // split-K reduction: partial chunk landed in ring slot
   uint32_t tmem_base;
@@ -182,6 +181,25 @@ __device__ __forceinline__ void epilogue_sync() {  // warps 0-3 only
   asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
 }
 
+// Stage s's scales are in TMEM: the four scale warps arrive and the MMA warp
+// waits on hardware named barrier 2 + s.  A named barrier, not an mbarrier:
+// on B200 a shared-memory access by the warp that issues tcgen05.mma waits
+// for its queued MMAs to drain (measured: one mbarrier wait per four K=64
+// MMAs cost ~280 cycles), so the MMA warp touches no shared memory in its
+// loop.  At most one arrival per stage is outstanding: the scale warps reach
+// stage s again only after full[s] of the next round, which needs this
+// round's MMAs to have retired.
+constexpr int kStageBarrierBase = 2;
+constexpr int kStageBarrierThreads = kEpiThreads + 32;
+__device__ __forceinline__ void stage_arrive(int s) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(kStageBarrierBase + s), "n"(kStageBarrierThreads)
+               : "memory");
+}
+__device__ __forceinline__ void stage_wait(int s) {
+  asm volatile("bar.sync %0, %1;" ::"r"(kStageBarrierBase + s), "n"(kStageBarrierThreads)
+               : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -273,7 +291,6 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
-      mbar_init(&bars->sf_ready[s], kEpiThreads / 32);
     }
     mbar_init(&bars->acc_full, 1);
     for (int r = 0; r < kRedSlots; ++r) mbar_init(&bars->red_full[r], 1);
@@ -315,15 +332,13 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
     }
     __syncwarp();
   } else if (warp == kWarpMma) {
-    if (lane == 0) {
-      // ---------------- tensor-core issuer: MMAs only, the scales are already in TMEM
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % kStages;
-        const uint32_t parity = (kb / kStages) & 1;
-        if (!mbar_wait(&bars->sf_ready[s], parity) || !mbar_wait(&bars->full[s], parity)) {
-          record_error(status, 2);
-          break;
-        }
+    // ---------------- tensor-core issuer: MMAs only, the scales are already in TMEM.
+    // The whole warp meets the scale warps at each stage's named barrier;
+    // lane 0 issues.  Nothing in this loop reads or writes shared memory.
+    for (int kb = 0; kb < kblocks; ++kb) {
+      const int s = kb % kStages;
+      stage_wait(s);  // the scale warps saw full[s] and stored this stage's scales
+      if (lane == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;");
         uint8_t* st = smem + s * kStageBytes;
         const uint32_t a_base = smem_u32(st), b_base = smem_u32(st + kATile);
@@ -338,8 +353,9 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
         }
         mma_commit(&bars->empty[s]);
       }
-      mma_commit(&bars->acc_full);
+      __syncwarp();
     }
+    if (lane == 0) mma_commit(&bars->acc_full);
     __syncwarp();
   } else {
     // ---------------- scale factors: shared memory -> TMEM, one warp per lane quadrant.
@@ -374,8 +390,7 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
       tmem_st16(quad_base + kColSF + s * 32 + 16, rb);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->sf_ready[s]);
+      stage_arrive(s);
     }
 
     // ---------------- epilogue: warp w reads accumulator lanes 32w..32w+31
