@@ -101,10 +101,6 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                "r"(bytes)
@@ -622,11 +618,14 @@ int choose_splits(int64_t m, int64_t n, int64_t k, int device_sms) {
   // Split K only when the output tiles leave SMs idle and K is long enough
   // that every split keeps at least 8 K blocks: a split CTA's fixed cost
   // (prologue, pipeline fill, fp32 partial round trip) outweighs the gain on
-  // short K (measured on B200: K=4096 decode shapes ran slower split).
+  // short K.  Measured on B200, splitting pays for tiles of at most 32 valid
+  // rows (cheap reduction) or for grids of very few tiles; a 64..128-row
+  // decode tile runs faster unsplit on the 64-wide deep-ring configuration.
   const int64_t tiles = (n / 128) * ((m + kBM - 1) / kBM);
   const int64_t kblocks = k / 256;
   if (tiles >= device_sms || kblocks < 24) return 1;
-  int64_t s = (device_sms + tiles - 1) / tiles;
+  if (m > 32 && tiles * 8 > device_sms) return 1;
+  int64_t s = device_sms / tiles;  // one wave: every split CTA resident at once
   if (s > kblocks / 8) s = kblocks / 8;
   if (s > kMaxSplits) s = kMaxSplits;
   return s < 1 ? 1 : (int)s;
