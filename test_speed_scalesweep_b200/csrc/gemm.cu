@@ -61,14 +61,17 @@ constexpr int kMaxRedSlots = 8;
 //   stage, not by bytes.
 template <int BN, int STAGES>
 struct Tile {
-  static_assert(BN == 128 || BN == 64, "tile width");
+  static_assert(BN == 256 || BN == 128 || BN == 64, "tile width");
   static_assert(STAGES <= kMaxStages, "ring depth");
   static constexpr int kBTile = BN * kBKBytes;
-  static constexpr int kStageBytes = kATile + kBTile + 2 * kSFTile;
-  // accumulator (BN fp32 columns), then per stage 16 SFA + 16 SFB columns,
-  // allocated as a power of two
+  // 128-row scale slabs of B per tile (one for BN <= 128)
+  static constexpr int kSFBSlabs = BN > 128 ? BN / 128 : 1;
+  static constexpr int kStageBytes = kATile + kBTile + (1 + kSFBSlabs) * kSFTile;
+  // accumulator (BN fp32 columns), then per stage 16 SFA + 16 x slabs SFB
+  // columns, allocated as a power of two
   static constexpr int kColSF = BN;
-  static constexpr int kUsedCols = BN + STAGES * 32;
+  static constexpr int kSFStageCols = 16 + 16 * kSFBSlabs;
+  static constexpr int kUsedCols = BN + STAGES * kSFStageCols;
   static constexpr int kTmemCols = kUsedCols <= 128 ? 128 : (kUsedCols <= 256 ? 256 : 512);
   // CTAs sharing an SM: what the shared memory allows (two 3-stage rings)
   static constexpr int kCtasPerSm = STAGES <= 3 ? 2 : 1;
@@ -276,8 +279,10 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
   // a 128-row scale slab covers 128 / BN output tiles; the MMA reads this
   // tile's rows from TMEM columns (row % 128) / 32, so a 64-wide tile in the
   // upper half of its slab starts 2 columns in
-  const uint8_t* sfb_tile = sfb + (uint64_t)(n_tile / (128 / kBN)) * sf_row_stride;
-  const uint32_t sfb_col_shift = (uint32_t)((n_tile % (128 / kBN)) * (kBN / 32));
+  constexpr int kSFBSlabs = T::kSFBSlabs, kSFStageCols = T::kSFStageCols;
+  const uint8_t* sfb_tile = sfb + ((uint64_t)n_tile * kBN / 128) * sf_row_stride;
+  const uint32_t sfb_col_shift =
+      kBN < 128 ? (uint32_t)((n_tile % (128 / (kBN < 128 ? kBN : 128))) * (kBN / 32)) : 0u;
   // A single, partial M tile (decode batches) loads only its rows, rounded up
   // to the 8-row swizzle atom; the stale rows after them only reach output
   // rows that are never stored.  Saves tile ingress when it is the bound.
@@ -322,8 +327,11 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
         tma_load_2d(st + kATile, &map_b, &bars->full[s], gkb * kBKBytes, n_tile * kBN);
         bulk_load(st + kATile + kBTile, sfa_tile + (uint64_t)gkb * kSFTile, kSFTile,
                   &bars->full[s]);
-        bulk_load(st + kATile + kBTile + kSFTile, sfb_tile + (uint64_t)gkb * kSFTile, kSFTile,
-                  &bars->full[s]);
+#pragma unroll
+        for (int slab = 0; slab < kSFBSlabs; ++slab)
+          bulk_load(st + kATile + kBTile + (1 + slab) * kSFTile,
+                    sfb_tile + slab * sf_row_stride + (uint64_t)gkb * kSFTile, kSFTile,
+                    &bars->full[s]);
       }
     }
     __syncwarp();
@@ -338,13 +346,15 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
         asm volatile("tcgen05.fence::after_thread_sync;");
         uint8_t* st = smem + s * kStageBytes;
         const uint32_t a_base = smem_u32(st), b_base = smem_u32(st + kATile);
-        const uint32_t col_sfa = tmem + kColSF + s * 32, col_sfb = col_sfa + 16 + sfb_col_shift;
+        const uint32_t col_sfa = tmem + kColSF + s * kSFStageCols;
+        const uint32_t col_sfb = col_sfa + 16 + sfb_col_shift;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           // K step j: 64 fp4 values = 32 bytes into each 128-byte swizzled row
           const uint64_t adesc = smem_desc(a_base + 32 * j, 16, 1024, kLayoutSW128);
           const uint64_t bdesc = smem_desc(b_base + 32 * j, 16, 1024, kLayoutSW128);
-          mma_nvf4(tmem, adesc, bdesc, T::kIdesc, col_sfa + 4 * j, col_sfb + 4 * j,
+          // step j's B scales: 4 columns per 128-row slab
+          mma_nvf4(tmem, adesc, bdesc, T::kIdesc, col_sfa + 4 * j, col_sfb + 4 * kSFBSlabs * j,
                    (kb | j) != 0);
         }
         mma_commit(&bars->empty[s]);
@@ -367,23 +377,31 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
         record_error(status, 6);
         sf_ok = false;
       }
-      uint32_t ra[16], rb[16];
+      // SFA: columns 4j..4j+3.  SFB: per step j, 4 columns per 128-row slab.
+      uint32_t ra[16], rb[16 * kSFBSlabs];
       const uint8_t* sf_st = smem + s * kStageBytes + kATile + kBTile;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        uint4 a4 = make_uint4(0u, 0u, 0u, 0u), b4 = make_uint4(0u, 0u, 0u, 0u);
-        if (sf_ok) {
-          a4 = *reinterpret_cast<const uint4*>(sf_st + 512 * j + 16 * lane);
-          b4 = *reinterpret_cast<const uint4*>(sf_st + kSFTile + 512 * j + 16 * lane);
-        }
+        uint4 a4 = make_uint4(0u, 0u, 0u, 0u);
+        if (sf_ok) a4 = *reinterpret_cast<const uint4*>(sf_st + 512 * j + 16 * lane);
         ra[4 * j] = a4.x, ra[4 * j + 1] = a4.y, ra[4 * j + 2] = a4.z, ra[4 * j + 3] = a4.w;
-        rb[4 * j] = b4.x, rb[4 * j + 1] = b4.y, rb[4 * j + 2] = b4.z, rb[4 * j + 3] = b4.w;
+#pragma unroll
+        for (int slab = 0; slab < kSFBSlabs; ++slab) {
+          uint4 b4 = make_uint4(0u, 0u, 0u, 0u);
+          if (sf_ok)
+            b4 = *reinterpret_cast<const uint4*>(sf_st + (1 + slab) * kSFTile + 512 * j + 16 * lane);
+          uint32_t* d = rb + 4 * (kSFBSlabs * j + slab);
+          d[0] = b4.x, d[1] = b4.y, d[2] = b4.z, d[3] = b4.w;
+        }
       }
       // the previous user of these columns (K block kb - kStages) has finished:
       // full[s] for this round completes only after the producer saw its MMAs
       // retire through empty[s]
-      tmem_st16(quad_base + kColSF + s * 32, ra);
-      tmem_st16(quad_base + kColSF + s * 32 + 16, rb);
+      const uint32_t stage_cols = quad_base + kColSF + s * kSFStageCols;
+      tmem_st16(stage_cols, ra);
+#pragma unroll
+      for (int h = 0; h < kSFBSlabs; ++h)
+        tmem_st16(stage_cols + 16 + 16 * h, *reinterpret_cast<const uint32_t(*)[16]>(rb + 16 * h));
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;");
       stage_arrive(s);
@@ -632,6 +650,13 @@ int choose_splits(int64_t m, int64_t n, int64_t k, int device_sms) {
 }
 
 int choose_tile_n(int64_t m, int64_t n, int splits, int device_sms) {
+  // Enough 128x256 tiles to give every SM one: the wide tile carries 25%
+  // fewer tile bytes per FLOP (A is shared by 256 columns), and tile ingress
+  // bounds the large-M GEMM.  It takes a whole SM (216 KiB ring, 448 TMEM
+  // columns).
+  if (splits <= 1 && m > kBM && n % 256 == 0 &&
+      (n / 256) * ((m + kBM - 1) / kBM) >= device_sms)
+    return 256;
   // A single M tile whose 128-wide N tiles do not fill the SMs streams its
   // weights through twice as many 64-wide tiles (each CTA's TMA stream is
   // latency-bound, so more CTAs move more bytes).  Split-K keeps 128.
@@ -698,7 +723,9 @@ cudaError_t launch(const GemmArgs& g, int splits, cudaStream_t stream, const cha
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (choose_tile_n(g.m, g.n, splits, sms) == 64) return launch_bn<64, 7>(g, 1, stream, why);
+  const int tile_n = choose_tile_n(g.m, g.n, splits, sms);
+  if (tile_n == 256) return launch_bn<256, 4>(g, 1, stream, why);
+  if (tile_n == 64) return launch_bn<64, 7>(g, 1, stream, why);
   return launch_bn<128, 3>(g, splits, stream, why);
 }
 

@@ -34,8 +34,11 @@ def _rel_fro(got, ref):
     return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
 
 
+# (2000, 2560, 512): 128x256 tiles (16 x 10 = 160 of them fill the SMs), last M
+# tile partial; (64, 4096, 1024): 128x64 tiles, upper-half scale columns
 @pytest.mark.parametrize("m,n,k", [(128, 128, 256), (16, 256, 512), (200, 384, 1024),
-                                   (1, 128, 4096), (1024, 512, 4096)])
+                                   (1, 128, 4096), (1024, 512, 4096), (2000, 2560, 512),
+                                   (64, 4096, 1024)])
 def test_gemm_matches_dequant_matmul_oracle(lib, m, n, k):
     from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm
     _, gsi_a, qa, sa = _quantized(m, k, 1 + m, 1.0, "scalesweep_mse")
@@ -51,7 +54,8 @@ def test_gemm_matches_dequant_matmul_oracle(lib, m, n, k):
     assert err <= TOL, err
 
 
-@pytest.mark.parametrize("m,n,k", [(16, 6144, 4096), (128, 4096, 4096), (1024, 4096, 14336)])
+@pytest.mark.parametrize("m,n,k", [(16, 6144, 4096), (128, 4096, 4096), (1024, 4096, 14336),
+                                   (8192, 4096, 4096)])
 def test_gemm_matches_vllm_cutlass_fp4_gemm(lib, m, n, k):
     vops = pytest.importorskip("vllm._custom_ops")
     if not hasattr(torch.ops, "_C") or not hasattr(torch.ops._C, "cutlass_scaled_fp4_mm"):
