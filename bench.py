@@ -228,6 +228,52 @@ def graph_avg_ms(fn, reps: int, device) -> float:
     return ms
 
 
+def dequant_mse(x, codes, scales, gsi) -> float:
+    """Mean squared error of the dequantized NVFP4 result against the input,
+    the quality figure the reference reports per backend.  Plain torch on the
+    GPU: E2M1 lookup, E4M3 scales read through the 128x4 swizzle."""
+    import torch
+    m, n = x.shape
+    dev = x.device
+    lut = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
+                        -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0], device=dev)
+    c = codes.view(torch.uint8).to(torch.int64)
+    vals = torch.stack([lut[c & 0xF], lut[c >> 4]], dim=-1).reshape(m, n)
+    kb = n // 16
+    kpad = (kb + 3) // 4 * 4
+    r = torch.arange(m, device=dev)[:, None]
+    col = torch.arange(kb, device=dev)[None, :]
+    off = (r >> 7) * (kpad * 128) + (col >> 2) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (col & 3)
+    sb = scales.view(torch.uint8).reshape(-1)[off]
+    s = sb.view(torch.float8_e4m3fn).to(torch.float32)
+    deq = vals.reshape(m, kb, 16) * (s / gsi.reshape(1)).unsqueeze(-1)
+    return float((deq.reshape(m, n) - x.float()).square().mean().item())
+
+
+def run_quality(device):
+    """Dequantized MSE on N(0,1) bf16 [M, 4096], the reference's quality
+    benchmark: fp8_max 256 for the scale-sweep backends, 448 for RTN."""
+    import torch
+    from test_speed_scalesweep_b200 import custom
+    out = {"input": "torch.randn bf16 [M, 4096], seeded; gsi = fp8_max*6/amax"}
+    g = torch.Generator(device=device).manual_seed(1234)
+    backends = (("scalesweep_mse", 256.0), ("scalesweep_mse_reference", 256.0), ("rtn", 448.0),
+                ("cutlass", 448.0))
+    for m in (1024, 8192):
+        x = torch.randn(m, 4096, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+        row = {}
+        for backend, fp8_max in backends:
+            gsi = ((fp8_max * 6.0) / x.abs().max().to(torch.float32)).reshape(1)
+            try:
+                codes, scales = custom.nvfp4_quant(x, gsi, True, backend)
+            except Exception as exc:  # vLLM's comparator may be missing
+                row[backend] = f"unavailable: {type(exc).__name__}"
+                continue
+            row[backend] = round(dequant_mse(x, codes, scales, gsi), 8)
+        out[f"M{m}_K4096"] = row
+    return out
+
+
 def run_sweep(device, reps: int = 20):
     """Standalone quantizer at the shape-sweep configs, scale-sweep vs RTN."""
     import torch
@@ -526,6 +572,7 @@ def run_ours(args):
     sweep = None
     cpu = None
     gemm_res = None
+    quality = None
     if rank == 0 and world == 1:
         del x
         torch.cuda.empty_cache()
@@ -533,6 +580,7 @@ def run_ours(args):
             sweep = run_sweep(device)
         if not args.no_gemm:
             gemm_res = run_gemm_sweep(device)
+        quality = run_quality(device)
         if not args.no_cpu:
             cpu = cpu_sample_rate(args.rows)
 
@@ -553,6 +601,8 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         if sweep is not None:
             line["sweep"] = sweep
+        if quality is not None:
+            line["quality_mse"] = quality
         if gemm_res is not None:
             line["gemm"] = gemm_res
         print(json.dumps(line), flush=True)
