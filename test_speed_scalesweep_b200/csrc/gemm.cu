@@ -8,22 +8,26 @@
 // the operation vLLM's cutlass_scaled_fp4_mm performs for a W4A4 linear layer
 // (vllm 0.22 model_executor/kernels/linear/nvfp4/cutlass.py:64-71).
 //
-// One CTA computes one 128 x 128 output tile:
-//   warp 0 (one lane)  : producer.  TMA tiled loads of the A and B code tiles
-//                        (128 rows x 128 bytes, 128B swizzle; no multicast)
-//                        and 1-D bulk copies of the four 512-byte scale atoms
-//                        of each operand per 256-wide K block, into a
-//                        3-stage shared-memory ring guarded by mbarriers.
-//   Two CTAs share an SM (110 KiB shared memory and 256 TMEM columns each), so
-//   one CTA's epilogue overlaps the other's main loop.
-//   warp 1 (one lane)  : tensor-core issuer.  Copies each stage's scale atoms
-//                        to TMEM (tcgen05.cp 32x128b.warpx4), then issues
+// One CTA computes one 128 x BN output tile (BN = 256, 128 or 64, chosen per
+// problem; see choose_tile_n) with six warps:
+//   warp 4 (one lane)  : producer.  TMA tiled loads of the A and B code tiles
+//                        (128B swizzle; no multicast) and 1-D bulk copies of
+//                        the 512-byte scale atoms of each operand per
+//                        256-deep K block, into a shared-memory ring guarded
+//                        by mbarriers.
+//   warps 0-3          : scale factors, then epilogue.  Per stage they copy
+//                        the scale atoms from shared memory into that stage's
+//                        TMEM columns with tcgen05.st (warp w owns TMEM lanes
+//                        32w..32w+31), then arrive on the stage's hardware
+//                        named barrier.  After the main loop: tcgen05.ld of
+//                        the fp32 accumulator, x alpha, round to bf16, store.
+//   warp 5             : TMEM allocation and the tensor-core issue stream:
 //                        4 x tcgen05.mma kind::mxf4nvf4.block_scale.block16
-//                        (M=128, N=128, K=64) accumulating fp32 in TMEM, and
-//                        releases the stage with tcgen05.commit.
-//   warps 0-3          : epilogue.  tcgen05.ld of the 128 x 128 fp32
-//                        accumulator (one TMEM lane quadrant per warp),
-//                        x alpha, round to bf16, store.
+//                        (M=128, N=BN, K=64) per K block, released with
+//                        tcgen05.commit.  It waits on named barriers only and
+//                        never touches shared memory inside its loop: on B200
+//                        a shared-memory access by the issuing warp waits for
+//                        its queued MMAs to drain.
 // Every mbarrier wait is bounded; a wait that gives up records an error code
 // in *status and the CTA still frees its TMEM before returning.
 #include <cstdint>
