@@ -580,7 +580,8 @@ def run_ours(args):
             sweep = run_sweep(device)
         if not args.no_gemm:
             gemm_res = run_gemm_sweep(device)
-        quality = run_quality(device)
+        if not args.no_sweep:
+            quality = run_quality(device)
         if not args.no_cpu:
             cpu = cpu_sample_rate(args.rows)
 
