@@ -32,6 +32,10 @@ def cutlass_scaled_fp4_mm(a: torch.Tensor, b: torch.Tensor, block_scale_a: torch
             raise ValueError(f"{name} must be a CUDA tensor")
         if not t.is_contiguous():
             raise ValueError(f"{name} must be contiguous")
+        if t.device != a.device:
+            raise ValueError(f"{name} must be on {a.device}, got {t.device}")
+    if status is not None and (status.device != a.device or status.dtype != torch.int32):
+        raise ValueError(f"status must be an int32 tensor on {a.device}")
     if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
         raise ValueError("a [M, K/2] and b [N, K/2] must share K")
     m, n, k = a.shape[0], b.shape[0], a.shape[1] * 2
