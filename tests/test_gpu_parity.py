@@ -287,3 +287,51 @@ def test_registered_ops_and_cuda_graph_capture(lib):
     torch.cuda.synchronize()
     assert torch.equal(out, c_eager)
     assert torch.equal(osc.view(torch.uint8), s_eager.view(torch.uint8))
+
+
+def _random_case(i):
+    """Seeded random configuration: shape (ragged K, padded_n, misaligned
+    rows), dtype, variant, layout and input distribution, with NaN / inf /
+    zero / denormal specials sprinkled in some cases."""
+    rng = np.random.default_rng(9000 + i)
+    kind = ["mse", "reference", "weighted", "rtn", "mse", "reference"][i % 6]
+    if i % 8 == 7:
+        kind = "mse128" if i % 16 == 7 else "weighted128"
+    small = kind in ("mse128", "weighted128")
+    m = int(rng.integers(1, 64 if small else 700))
+    k = 16 * int(rng.integers(1, 32 if small else 400))
+    pn = k + 16 * int(rng.integers(0, 5)) if rng.random() < 0.3 else k
+    dtype = "f16" if rng.random() < 0.25 else "bf16"
+    swz = bool(rng.random() < 0.7)
+    if rng.random() < 0.5:
+        x = gi.wide_range_activations(m, k, 100 + i, dtype)
+    else:
+        x = gi.outlier_activations(m, k, 100 + i, dtype)
+    if rng.random() < 0.3:
+        specials = np.array([0x7FC0, 0x7F80, 0xFF80, 0x0000, 0x8000, 0x0001, 0x8003]
+                            if dtype == "bf16" else
+                            [0x7E00, 0x7C00, 0xFC00, 0x0000, 0x8000, 0x0001, 0x8003], np.uint16)
+        flat = x.reshape(-1)
+        idx = rng.choice(flat.size, size=min(flat.size, 1 + flat.size // 97), replace=False)
+        flat[idx] = rng.choice(specials, size=idx.size)
+    return kind, m, k, pn, dtype, swz, x
+
+
+@pytest.mark.parametrize("i", range(48))
+def test_random_configurations_match_oracle(lib, i):
+    kind, m, k, pn, dtype, swz, x = _random_case(i)
+    if kind == "reference" and pn != k:
+        pn = k  # the reference variant has no padded_n (it raises)
+    finite = gi.bits_to_f32(x, dtype)
+    finite = finite[np.isfinite(finite)]
+    amax = float(np.abs(finite).max()) if finite.size else 1.0
+    gsi = float(np.float32(2688.0) / np.float32(amax if amax > 0 else 1.0))
+    codes, scales = c_quant(lib, kind, to_device(x, dtype), gsi, padded_n=pn if pn != k else None,
+                            swizzled=swz)
+    variant = {"mse": "mse", "reference": "reference", "weighted": "weighted", "rtn": "mse",
+               "mse128": "mse", "weighted128": "weighted"}[kind]
+    mode = {"rtn": "rtn", "mse128": "full_range", "weighted128": "full_range"}.get(kind, "window")
+    oc, os_ = oracle.quantize(x, gsi, dtype=dtype, padded_n=pn if pn != k else None,
+                              swizzled=swz, variant=variant, mode=mode)
+    np.testing.assert_array_equal(codes, oc)
+    np.testing.assert_array_equal(scales, os_)
