@@ -372,10 +372,26 @@ def cpu_sample_rate(rows_hint: int, budget_s: float = 12.0):
     t = time.perf_counter()
     oracle.quantize(x, gsi, nthreads=threads)
     dt = time.perf_counter() - t
+    # config 1 (128 x 4096) and the config-2 shapes with M <= 1024 at K = 4096:
+    # median of 5 runs after one warm-up, ms per call
+    shapes = {}
+    for m, k in ((128, 4096), (1, 4096), (16, 4096), (64, 4096), (256, 4096), (1024, 4096)):
+        xs = gi.outlier_activations(m, k, seed=4300 + m)
+        g = gi.torch_style_gsi(xs, FP8_MAX)
+        oracle.quantize(xs, g, nthreads=threads)
+        times = []
+        for _ in range(5):
+            t = time.perf_counter()
+            oracle.quantize(xs, g, nthreads=threads)
+            times.append(time.perf_counter() - t)
+        ms = sorted(times)[2] * 1e3
+        shapes[f"{m}x{k}"] = {"ms": round(ms, 4),
+                              "GB/s": round(m * k * BYTES_PER_ELEM / (ms * 1e-3) / 1e9, 4)}
     return {"value": round(rows * K_DIM * BYTES_PER_ELEM / dt / 1e9, 4), "unit": UNIT,
             "cores": threads, "kind": "port",
             "sample": f"{rows} x {K_DIM} rows of the workload ({rows * K_DIM // 16} blocks), "
-                      f"{dt:.2f} s, oracle/scalesweep_oracle.c with {threads} OpenMP threads"}
+                      f"{dt:.2f} s, oracle/scalesweep_oracle.c with {threads} OpenMP threads",
+            "shapes": shapes}
 
 
 def run_reference(args):
