@@ -8,8 +8,12 @@
 // the operation vLLM's cutlass_scaled_fp4_mm performs for a W4A4 linear layer
 // (vllm 0.22 model_executor/kernels/linear/nvfp4/cutlass.py:64-71).
 //
-// One CTA computes one 128 x BN output tile (BN = 256, 128 or 64, chosen per
-// problem; see choose_tile_n) with six warps:
+// Two kernels, chosen per problem by choose_tile_n:
+// - nvfp4_gemm_pair_kernel (large M, more 256 x 256 tiles than SM pairs):
+//   persistent clusters of two CTAs sharing each 256 x 256 tile through
+//   tcgen05.mma.cta_group::2; described at its definition.
+// - nvfp4_gemm_kernel: one CTA computes one 128 x BN output tile (BN = 256,
+//   128 or 64) with six warps:
 //   warp 4 (one lane)  : producer.  TMA tiled loads of the A and B code tiles
 //                        (128B swizzle; no multicast) and 1-D bulk copies of
 //                        the 512-byte scale atoms of each operand per
@@ -594,6 +598,456 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Pair configuration (large M): clusters of two CTAs on two SMs, persistent
+// over 256 x 256 output tiles, with tcgen05.mma.cta_group::2 (M=256, N=256,
+// K=64).  For each tile each CTA loads its own 128 rows of A and 128 of the
+// tile's 256 rows of B; the leader (cluster rank 0) issues one MMA stream that
+// reads both CTAs' shared memory at the same offsets and writes rows 0-127 of
+// D into the leader's TMEM and rows 128-255 into the peer's.  Per 256-deep K
+// block each SM moves 32 KiB of code tiles for a 128 x 256 share of the
+// output, against 48 KiB in a one-CTA 128 x 256 tile; L2-to-shared-memory
+// ingress is what bounds these shapes.
+// Scales (measured on B200): each CTA's TMEM holds the A scales of its own 128
+// rows (4 columns per K=64 step) and the B scales of all 256 tile rows (8
+// columns per step), the columns the one-CTA 256-wide tile uses.
+//
+// Warps (both CTAs; 15 warps):
+//   0-3   scale factors: shared memory -> this CTA's TMEM (warp w owns lanes
+//         32w..32w+31)
+//   4-11  epilogue, two warps per TMEM lane quadrant (w % 4), 128 columns
+//         each: TMEM -> registers (bf16), release the accumulator, then per
+//         32 x 32 block through a swizzled shared-memory buffer to global,
+//         8 rows x 64 B per store instruction, while the next tile's main
+//         loop runs.  Measured on B200: stores straight from registers (32
+//         rows per instruction) stalled the next tile's start by ~1.6 us, and
+//         TMA stores slowed the main loop's TMA loads by ~12%.
+//   12    producer (one lane): this CTA's tiles and scale atoms by TMA
+//   13    TMEM allocation; in the leader the MMA issue stream
+//   14    leader only, gate: waits until the peer's stage is ready
+// TMEM (512 columns): accumulator 0-255, scale factors 256-495 (5 stages).
+// With one accumulator the MMAs of the next tile wait for the epilogue's
+// TMEM reads, not for its global stores.
+//
+// Barriers (every wait bounded; stage ring and tile counters continue across
+// tiles):
+//   full[s]      each CTA: its own A/B tiles and scale atoms landed (its own
+//                loads complete on it; a TMA load completing on the other
+//                CTA's barrier stalled the issuing CTA's later copies on B200)
+//   peer_rdy[s]  leader: the peer's four scale warps saw the peer's full[s]
+//                and stored its scales in TMEM (remote arrivals)
+//   empty[s]     each CTA: the MMAs of stage s retired (one commit per CTA)
+//   acc_full     each CTA: its half of the accumulator is final (per tile)
+//   acc_empty    leader: all eight epilogue warps of the pair read the
+//                accumulator (4 local + 4 remote arrivals, per tile)
+// The gate, the leader's scale warps and the MMA warp meet on the stage's
+// hardware named barrier, so the MMA warp waits on mbarriers only at tile
+// boundaries, where its queue drains anyway.  Waits on barriers that the
+// other CTA signals spin on test_wait with acquire at cluster scope (a
+// suspended try_wait woke ~0.4 us late after a remote arrival on B200); the
+// remote arrivals are relaxed (see mbar_arrive_cluster_relaxed).
+constexpr int kPairStages = 5;
+constexpr int kTilePair = 512;  // choose_tile_n's code for the pair configuration
+constexpr int kPairThreads = 480;
+constexpr int kPairWarpEpi = 4, kPairEpiWarps = 8;
+constexpr int kPairWarpProducer = 12, kPairWarpMma = 13, kPairWarpGate = 14;
+// epilogue staging: one 32 x 32 bf16 block per epilogue warp, its 16-byte
+// chunks XOR-swizzled by row so both the row writes and the coalesced reads
+// are free of bank conflicts
+constexpr int kPairStoreBlock = 32 * 32 * 2;
+constexpr int kPairStoreBytes = kPairEpiWarps * kPairStoreBlock;
+constexpr int kPairStageThreads = kEpiThreads + 64;  // scale warps + gate + MMA
+struct PairTile {
+  static constexpr int kStageBytes = kATile + kBM * kBKBytes + 3 * kSFTile;  // A, B half, 3 atoms
+  static constexpr int kColSF = 256;
+  static constexpr int kSFStageCols = 48;  // 16 SFA + 32 SFB (two 128-row slabs)
+  static constexpr int kTmemCols = 512;
+  static_assert(kColSF + kPairStages * kSFStageCols <= kTmemCols, "TMEM columns");
+  // M=256 (M>>4 = 16), N=256 (N>>3 = 32); otherwise as Tile::kIdesc
+  static constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | (32u << 17) | (16u << 24);
+};
+
+struct __align__(8) PairBarriers {
+  uint64_t full[kMaxStages];
+  uint64_t peer_rdy[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t acc_full;
+  uint64_t acc_empty;
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The shared::cluster address of the same shared-memory offset in CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_local(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Relaxed remote arrival.  Its callers publish tcgen05 data movement (stores
+// of scales, loads of the accumulator) that they have waited for
+// (tcgen05.wait::st / ::ld) and ordered before the arrival with
+// tcgen05.fence::before_thread_sync; they have no generic-proxy writes for a
+// release to carry.  A release at cluster scope (like fence.acq_rel.cluster)
+// held the arriving warp ~0.6 us per arrival on B200, which serialised the
+// peer's stages.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// Bounded wait for barriers the other CTA signals: a non-suspending
+// test_wait spin with acquire at cluster scope (no separate fence).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void mma_nvf4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t sfa_tmem,
+                                              uint32_t sfb_tmem, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], "
+      "[%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum), "r"(sfa_tmem), "r"(sfb_tmem));
+}
+
+// Pair stage barrier: the leader's scale warps and gate warp arrive, the MMA
+// warp waits (hardware named barrier 2 + s, 192 threads).
+__device__ __forceinline__ void pair_stage_arrive(int s) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(kStageBarrierBase + s), "n"(kPairStageThreads)
+               : "memory");
+}
+__device__ __forceinline__ void pair_stage_wait(int s) {
+  asm volatile("bar.sync %0, %1;" ::"r"(kStageBarrierBase + s), "n"(kPairStageThreads)
+               : "memory");
+}
+
+// Arrive on a barrier (shared::cluster address, either CTA) once this
+// thread's pair MMAs retire.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+// 256-row x 256-column tile t of a grid with n_pairs tiles per row.
+struct PairTileCoord {
+  int m_pair, n_pair;
+};
+__device__ __forceinline__ PairTileCoord pair_tile_coord(int t, int n_pairs) {
+  return {t / n_pairs, t % n_pairs};
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+    nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
+                           const __grid_constant__ CUtensorMap map_b,
+                           const uint8_t* __restrict__ sfa, const uint8_t* __restrict__ sfb,
+                           const float* __restrict__ alpha_ptr, __nv_bfloat16* __restrict__ out,
+                           int m, int n, int k, int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // same 1024-aligned offsets in both CTAs: the pair MMA reads the peer's
+  // tiles at the leader's descriptor addresses
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  using T = PairTile;
+  constexpr int kStages = kPairStages, kStageBytes = T::kStageBytes;
+  constexpr int kBHalfOff = kATile, kSFOff = kATile + kBM * kBKBytes;
+  uint8_t* store_buf = smem + kStages * kStageBytes;  // 1024-aligned
+  PairBarriers* bars =
+      reinterpret_cast<PairBarriers*>(smem + kStages * kStageBytes + kPairStoreBytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  // tiles cluster_id, cluster_id + clusters, ... (both CTAs walk the same list)
+  const int cluster_id = (int)(blockIdx.x >> 1), clusters = (int)(gridDim.x >> 1);
+  const int n_pairs = n / 256, tiles = n_pairs * ((m + 2 * kBM - 1) / (2 * kBM));
+  const int kblocks = k / 256;
+  const uint64_t sf_row_stride = (uint64_t)(k / 16) * 128;
+  const int m_slabs = (m + kBM - 1) / kBM;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->peer_rdy[s], 4);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, 2 * kPairEpiWarps);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)));
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)));
+  }
+  if (warp == kPairWarpMma) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&bars->tmem_base)),
+                 "n"(T::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers are initialised before any remote arrival
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == kPairWarpProducer) {
+    if (lane == 0) {
+      // ---------------- producer (both CTAs): this CTA's tiles and scales
+      int it = 0;  // stage counter, continued across tiles
+      bool ok = true;
+      for (int t = cluster_id; t < tiles && ok; t += clusters) {
+        const PairTileCoord tc = pair_tile_coord(t, n_pairs);
+        // The upper CTA of a last pair tile may lie wholly past M: it still
+        // supplies its B rows, its A box reads the TMA fill and its A scales
+        // come from the last slab (rows that are never stored).
+        const int m_half = tc.m_pair * 2 + (int)rank;
+        const uint8_t* sfa_tile = sfa + (uint64_t)min(m_half, m_slabs - 1) * sf_row_stride;
+        const uint8_t* sfb_tile = sfb + (uint64_t)(tc.n_pair * 2) * sf_row_stride;
+        const int b_row = (tc.n_pair * 2 + (int)rank) * kBM;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t round = it / kStages;
+          // the peer's empty[s] is signalled by the leader's commit
+          if (round > 0 && !mbar_wait(&bars->empty[s], (round - 1) & 1)) {
+            record_error(status, 1);
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * kStageBytes;
+          uint64_t* full = &bars->full[s];
+          mbar_expect_tx(full, kStageBytes);
+          tma_load_2d(st, &map_a, full, kb * kBKBytes, m_half * kBM);
+          tma_load_2d(st + kBHalfOff, &map_b, full, kb * kBKBytes, b_row);
+          bulk_load(st + kSFOff, sfa_tile + (uint64_t)kb * kSFTile, kSFTile, full);
+          bulk_load(st + kSFOff + kSFTile, sfb_tile + (uint64_t)kb * kSFTile, kSFTile, full);
+          bulk_load(st + kSFOff + 2 * kSFTile, sfb_tile + sf_row_stride + (uint64_t)kb * kSFTile,
+                    kSFTile, full);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kPairWarpMma) {
+    if (rank == 0) {
+      // ---------------- pair MMA issuer (leader only)
+      const uint32_t empty_own = smem_u32(&bars->empty[0]);
+      const uint32_t empty_peer = cluster_addr(empty_own, 1);
+      const uint32_t acc_own = smem_u32(&bars->acc_full);
+      const uint32_t acc_peer = cluster_addr(acc_own, 1);
+      int it = 0, ti = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < tiles; t += clusters, ++ti) {
+        // both CTAs' epilogue warps have read the previous tile's accumulator
+        if (ti > 0) {
+          if (lane == 0 && ok && !mbar_wait_cluster(&bars->acc_empty, (uint32_t)(ti - 1) & 1u)) {
+            record_error(status, 9);
+            ok = false;
+          }
+          __syncwarp();
+        }
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % kStages;
+          pair_stage_wait(s);  // both CTAs' tiles landed and both CTAs' scales are in TMEM
+          if (lane == 0) {
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            uint8_t* st = smem + s * kStageBytes;
+            const uint32_t a_base = smem_u32(st), b_base = smem_u32(st + kBHalfOff);
+            const uint32_t col_sfa = tmem + T::kColSF + s * T::kSFStageCols;
+            const uint32_t col_sfb = col_sfa + 16;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint64_t adesc = smem_desc(a_base + 32 * j, 16, 1024, kLayoutSW128);
+              const uint64_t bdesc = smem_desc(b_base + 32 * j, 16, 1024, kLayoutSW128);
+              mma_nvf4_pair(tmem, adesc, bdesc, T::kIdesc, col_sfa + 4 * j, col_sfb + 8 * j,
+                            (kb | j) != 0);
+            }
+            const uint32_t off = (uint32_t)(s * sizeof(uint64_t));
+            mma_commit_pair(empty_own + off);
+            mma_commit_pair(empty_peer + off);
+          }
+          __syncwarp();
+        }
+        if (lane == 0) {
+          mma_commit_pair(acc_own);
+          mma_commit_pair(acc_peer);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == kPairWarpGate) {
+    if (rank == 0) {
+      // ---------------- gate (leader): the peer's stage is ready
+      bool ok = true;
+      int it = 0;
+      for (int t = cluster_id; t < tiles; t += clusters) {
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t parity = (uint32_t)(it / kStages) & 1u;
+          if (lane == 0 && ok && !mbar_wait_cluster(&bars->peer_rdy[s], parity)) {
+            record_error(status, 8);
+            ok = false;
+          }
+          __syncwarp();
+          pair_stage_arrive(s);
+        }
+      }
+    }
+  } else if (warp < kPairWarpEpi) {
+    // ---------------- scale factors (both CTAs): shared memory -> TMEM
+    const uint32_t quad_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t peer_rdy0 = cluster_addr(smem_u32(&bars->peer_rdy[0]), 0);
+    bool sf_ok = true;
+    int it = 0;
+    for (int t = cluster_id; t < tiles; t += clusters) {
+      for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        const int s = it % kStages;
+        const uint32_t parity = (uint32_t)(it / kStages) & 1u;
+        if (sf_ok && !mbar_wait(&bars->full[s], parity)) {
+          record_error(status, 6);
+          sf_ok = false;
+        }
+        // SFA: columns 4j..4j+3.  SFB: 8 columns per step j, slab h at 4h.
+        uint32_t ra[16], rb[32];
+        const uint8_t* sf_st = smem + s * kStageBytes + kSFOff;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 a4 = make_uint4(0u, 0u, 0u, 0u);
+          if (sf_ok) a4 = *reinterpret_cast<const uint4*>(sf_st + 512 * j + 16 * lane);
+          ra[4 * j] = a4.x, ra[4 * j + 1] = a4.y, ra[4 * j + 2] = a4.z, ra[4 * j + 3] = a4.w;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint4 b4 = make_uint4(0u, 0u, 0u, 0u);
+            if (sf_ok)
+              b4 = *reinterpret_cast<const uint4*>(sf_st + (1 + h) * kSFTile + 512 * j +
+                                                   16 * lane);
+            uint32_t* d = rb + 4 * (2 * j + h);
+            d[0] = b4.x, d[1] = b4.y, d[2] = b4.z, d[3] = b4.w;
+          }
+        }
+        // columns free: full[s] of this round follows empty[s] of the last
+        const uint32_t stage_cols = quad_base + T::kColSF + s * T::kSFStageCols;
+        tmem_st16(stage_cols, ra);
+        tmem_st16(stage_cols + 16, *reinterpret_cast<const uint32_t(*)[16]>(rb));
+        tmem_st16(stage_cols + 32, *reinterpret_cast<const uint32_t(*)[16]>(rb + 16));
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;");
+        if (rank == 0) {
+          pair_stage_arrive(s);
+        } else {
+          __syncwarp();
+          // the peer's tiles landed (full[s]) and its scales are in TMEM
+          if (lane == 0)
+            mbar_arrive_cluster_relaxed(peer_rdy0 + (uint32_t)(s * sizeof(uint64_t)));
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): TMEM lanes 32q..32q+31, columns 128h..128h+127
+    const int e = warp - kPairWarpEpi, q = warp & 3, h = e >> 2;
+    const uint32_t quad = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 128);
+    const uint32_t acc_empty_leader = cluster_addr(smem_u32(&bars->acc_empty), 0);
+    uint8_t* blk = store_buf + e * kPairStoreBlock;
+    const float alpha = __ldg(alpha_ptr);
+    bool ok = true;
+    int ti = 0;
+    for (int t = cluster_id; t < tiles; t += clusters, ++ti) {
+      const PairTileCoord tc = pair_tile_coord(t, n_pairs);
+      uint32_t got = 0;
+      if (lane == 0 && ok) {
+        // the leader's acc_full is signalled by its own commit, the peer's remotely
+        got = (rank == 0 ? mbar_wait(&bars->acc_full, (uint32_t)ti & 1u)
+                         : mbar_wait_cluster(&bars->acc_full, (uint32_t)ti & 1u))
+                  ? 1u
+                  : 0u;
+        if (!got) record_error(status, 3);
+      }
+      const bool acc_ok = __shfl_sync(0xffffffffu, got, 0) != 0;
+      ok = ok && acc_ok;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      // this warp's 32 rows x 128 columns as bf16 pairs: 64 registers per lane
+      uint32_t packed[64];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(quad + (uint32_t)(c * 32), v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float lo = __uint_as_float(v[2 * i]) * alpha;
+          const float hi = __uint_as_float(v[2 * i + 1]) * alpha;
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed[16 * c + i]) : "f"(hi), "f"(lo));
+        }
+      }
+      // accumulator read: release it to the leader's MMA warp, then store
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0)
+          mbar_arrive_local(&bars->acc_empty);
+        else
+          mbar_arrive_cluster_relaxed(acc_empty_leader);
+      }
+      const int row0 = (tc.m_pair * 2 + (int)rank) * kBM + q * 32;
+      if (!acc_ok || row0 >= m) continue;  // rows past M: nothing to store
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        __syncwarp();  // previous block read back
+        // row `lane`: 16-byte chunk j at chunk j ^ ((row >> 1) & 3)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(blk + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16)) =
+              make_uint4(packed[16 * c + 4 * j], packed[16 * c + 4 * j + 1],
+                         packed[16 * c + 4 * j + 2], packed[16 * c + 4 * j + 3]);
+        __syncwarp();
+        // lanes 4r..4r+3 store the 64 bytes of row r (+8i): 8 rows per instruction
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = (lane >> 2) + 8 * i, j = lane & 3;
+          const uint4 v4 =
+              *reinterpret_cast<const uint4*>(blk + r * 64 + ((j ^ ((r >> 1) & 3)) * 16));
+          if (row0 + r < m)
+            *reinterpret_cast<uint4*>(out + (uint64_t)(row0 + r) * n + tc.n_pair * 256 +
+                                      h * 128 + c * 32 + j * 8) = v4;
+        }
+      }
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still touch its memory
+  if (warp == kPairWarpMma) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "n"(T::kTmemCols));
+  }
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -636,6 +1090,10 @@ size_t smem_bytes_for() {
 
 size_t smem_bytes() { return smem_bytes_for<128, 3>(); }
 
+size_t smem_bytes_pair() {
+  return kPairStages * PairTile::kStageBytes + kPairStoreBytes + sizeof(PairBarriers) + 1024;
+}
+
 int choose_splits(int64_t m, int64_t n, int64_t k, int device_sms) {
   // Split K only when the output tiles leave SMs idle and K is long enough
   // that every split keeps at least 8 K blocks: a split CTA's fixed cost
@@ -654,13 +1112,16 @@ int choose_splits(int64_t m, int64_t n, int64_t k, int device_sms) {
 }
 
 int choose_tile_n(int64_t m, int64_t n, int splits, int device_sms) {
-  // Enough 128x256 tiles to occupy most SMs (measured on B200: from ~60% of
-  // them the wide tile wins): it carries 25% fewer tile bytes per FLOP (A is
-  // shared by 256 columns), and tile ingress bounds these GEMMs.  It takes a
-  // whole SM (216 KiB ring, 448 TMEM columns).
-  if (splits <= 1 && m > kBM && n % 256 == 0 &&
-      (n / 256) * ((m + kBM - 1) / kBM) * 5 >= (int64_t)device_sms * 3)
-    return 256;
+  // 256-wide tiles: A is shared by 256 columns, and tile ingress bounds these
+  // GEMMs.  More 256 x 256 tiles than co-resident CTA pairs: the persistent
+  // pair kernel (its epilogue overlaps the next tile; measured on B200 it
+  // loses to the one-CTA tile when every pair gets a single tile).  Else,
+  // enough 128 x 256 tiles to occupy most SMs (from ~60% of them the wide
+  // tile wins): one CTA per 128 x 256 tile.
+  if (splits <= 1 && m > kBM && n % 256 == 0) {
+    if ((n / 256) * ((m + 2 * kBM - 1) / (2 * kBM)) > device_sms / 2) return kTilePair;
+    if ((n / 256) * ((m + kBM - 1) / kBM) * 5 >= (int64_t)device_sms * 3) return 256;
+  }
   // A single M tile whose 128-wide N tiles do not fill the SMs streams its
   // weights through twice as many 64-wide tiles (each CTA's TMA stream is
   // latency-bound, so more CTAs move more bytes).  Split-K keeps 128.
@@ -721,6 +1182,55 @@ cudaError_t launch_bn(const GemmArgs& g, int splits, cudaStream_t stream, const 
   return cudaGetLastError();
 }
 
+cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, const char** why) {
+  CUtensorMap map_a, map_b;
+  if (!make_code_map(&map_a, g.a, (uint64_t)g.m, (uint64_t)g.k / 2, kBM) ||
+      !make_code_map(&map_b, g.b, (uint64_t)g.n, (uint64_t)g.k / 2, kBM)) {
+    *why = "cuTensorMapEncodeTiled failed";
+    return cudaErrorInvalidValue;
+  }
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *why = "cudaGetDevice";
+    return e;
+  }
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    e = cudaFuncSetAttribute(nvfp4_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem_bytes_pair());
+    if (e != cudaSuccess) {
+      *why = "cudaFuncSetAttribute";
+      return e;
+    }
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  // persistent: one cluster per co-resident pair of SMs, at most one per tile
+  static int max_clusters[64] = {0};
+  int clusters = dev >= 0 && dev < 64 ? max_clusters[dev] : 0;
+  if (clusters <= 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem_bytes_pair();
+    if (cudaOccupancyMaxActiveClusters(&clusters, nvfp4_gemm_pair_kernel, &cfg) != cudaSuccess ||
+        clusters <= 0) {
+      cudaGetLastError();  // clear a failed query
+      int sms = 148;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      clusters = sms / 2;
+    }
+    if (dev >= 0 && dev < 64) max_clusters[dev] = clusters;
+  }
+  const int64_t tiles = (g.n / 256) * ((g.m + 2 * kBM - 1) / (2 * kBM));
+  if (tiles < clusters) clusters = (int)tiles;
+  dim3 grid((unsigned)clusters * 2, 1, 1);
+  nvfp4_gemm_pair_kernel<<<grid, kPairThreads, smem_bytes_pair(), stream>>>(
+      map_a, map_b, g.sfa, g.sfb, g.alpha, static_cast<__nv_bfloat16*>(g.out), (int)g.m,
+      (int)g.n, (int)g.k, g.status);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch(const GemmArgs& g, int splits, cudaStream_t stream, const char** why) {
@@ -728,6 +1238,7 @@ cudaError_t launch(const GemmArgs& g, int splits, cudaStream_t stream, const cha
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int tile_n = choose_tile_n(g.m, g.n, splits, sms);
+  if (tile_n == kTilePair) return launch_pair(g, stream, why);
   if (tile_n == 256) return launch_bn<256, 4>(g, 1, stream, why);
   if (tile_n == 64) return launch_bn<64, 7>(g, 1, stream, why);
   return launch_bn<128, 3>(g, splits, stream, why);

@@ -34,11 +34,17 @@ def _rel_fro(got, ref):
     return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
 
 
-# (2000, 2560, 512): 128x256 tiles (16 x 10 = 160 of them fill the SMs), last M
-# tile partial; (64, 4096, 1024): 128x64 tiles, upper-half scale columns
+# Persistent 256x256 CTA-pair tiles (more tiles than resident pairs):
+# (2000, 2560, 512) last pair's upper CTA partial; (1793, 2560, 512) its upper
+# CTA wholly past M (A scales from the last slab); (1970, 2560, 2048) upper CTA
+# 50 rows, K wraps the 5-stage ring; (1400, 4608, 768) three K blocks per tile
+# and two tiles for some pairs, so the ring wraps across tiles.
+# One-CTA 128x256 tiles: (1281, 2560, 512), (1458, 2560, 2048).
+# (64, 4096, 1024): 128x64 tiles, upper-half scale columns.
 @pytest.mark.parametrize("m,n,k", [(128, 128, 256), (16, 256, 512), (200, 384, 1024),
                                    (1, 128, 4096), (1024, 512, 4096), (2000, 2560, 512),
-                                   (64, 4096, 1024)])
+                                   (1793, 2560, 512), (1970, 2560, 2048), (1400, 4608, 768),
+                                   (1281, 2560, 512), (1458, 2560, 2048), (64, 4096, 1024)])
 def test_gemm_matches_dequant_matmul_oracle(lib, m, n, k):
     from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm
     _, gsi_a, qa, sa = _quantized(m, k, 1 + m, 1.0, "scalesweep_mse")
