@@ -299,6 +299,41 @@ def run_sweep(device, reps: int = 20):
     return out
 
 
+ACT_FUSION_M = (16, 128, 1024, 8192)
+ACT_FUSION_N = 14336  # Llama-3.1-8B intermediate width: the down projection's input
+
+
+def run_act_fusion_sweep(device, reps: int = 20):
+    """SiLU-and-mul + scalesweep_mse, unfused (two launches, bf16 intermediate
+    in HBM) against the fused kernel, on [M, 2 x 14336] gate_up outputs."""
+    import torch
+    from test_speed_scalesweep_b200 import act_quant
+    from test_speed_scalesweep_b200 import scalesweep_mse_nvfp4_utils as mse
+    n = ACT_FUSION_N
+    out = {"n": n, "method": "per-launch time from one CUDA graph of 20 launches"}
+    gsi = torch.tensor([FP8_MAX * 6.0 / 40.0], dtype=torch.float32, device=device)
+    for m in ACT_FUSION_M:
+        x = make_shard(m, 2 * n, 17 + m, device)
+        h = torch.empty(m, n, dtype=x.dtype, device=device)
+        codes, scales = act_quant.alloc_outputs(x, True)
+
+        def unfused():
+            act_quant.silu_and_mul(x, h)
+            mse.scalesweep_mse_nvfp4_quant_out(h, gsi, True, output=codes, output_scale=scales)
+
+        def fused():
+            act_quant.silu_and_mul_scalesweep_mse_nvfp4_quant_out(x, gsi, True, output=codes,
+                                                                  output_scale=scales)
+
+        u_ms = graph_avg_ms(unfused, reps, device)
+        f_ms = graph_avg_ms(fused, reps, device)
+        s_ms = graph_avg_ms(lambda: act_quant.silu_and_mul(x, h), reps, device)
+        out[f"M{m}"] = {"unfused_us": round(u_ms * 1e3, 2), "silu_and_mul_us": round(s_ms * 1e3, 2),
+                        "fused_us": round(f_ms * 1e3, 2), "speedup": round(u_ms / f_ms, 3)}
+        del x, h
+    return out
+
+
 def run_gemm_sweep(device, reps: int = 20):
     """Config 3: quantize + tcgen05 NVFP4 GEMM on the Llama-3.1-8B linear shapes.
 
@@ -589,6 +624,7 @@ def run_ours(args):
     cpu = None
     gemm_res = None
     quality = None
+    act_fusion = None
     if rank == 0 and world == 1:
         del x
         torch.cuda.empty_cache()
@@ -598,6 +634,7 @@ def run_ours(args):
             gemm_res = run_gemm_sweep(device)
         if not args.no_sweep:
             quality = run_quality(device)
+            act_fusion = run_act_fusion_sweep(device)
         if not args.no_cpu:
             cpu = cpu_sample_rate(args.rows)
 
@@ -622,6 +659,8 @@ def run_ours(args):
             line["quality_mse"] = quality
         if gemm_res is not None:
             line["gemm"] = gemm_res
+        if act_fusion is not None:
+            line["act_fusion"] = act_fusion
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

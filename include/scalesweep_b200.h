@@ -100,6 +100,37 @@ int ssw_scalesweep128_nvfp4_quant_out(const void* input, int input_dtype, int64_
                                       int is_sf_swizzled_layout, void* stream);
 
 /*
+ * SiLU-and-mul, the producer of the MLP down projection's activation:
+ *   output[r, c] = silu(input[r, c]) * input[r, n + c],  input [num_rows, 2n],
+ * output [num_rows, n], both bf16 or both f16.  silu(g) = g / (1 + e^-g) in
+ * binary32 (IEEE division), rounded to the input type; the product is rounded
+ * once.  Bit for bit what vLLM's silu_and_mul computes (vllm 0.22
+ * torch.ops._C.silu_and_mul, model_executor/layers/activation.py:117-147),
+ * checked on every bf16 and f16 gate value.  n % 16 == 0, input 32-byte and
+ * output 16-byte aligned, num_rows * n / 16 < 2^32.
+ */
+int ssw_silu_and_mul(const void* input, int input_dtype, int64_t num_rows, int64_t n,
+                     void* output, void* stream);
+
+/*
+ * SiLU-and-mul fused into the "scalesweep_mse" quantizer: the same codes and
+ * scales as ssw_scalesweep_mse_nvfp4_quant_out applied to the output of
+ * ssw_silu_and_mul, without writing that bf16 intermediate.  input is
+ * [num_rows, 2n] (gate, then up); output [num_rows, n/2]; no padding
+ * (physical_n = n).  Input 32-byte and output 8-byte aligned.
+ * This is the role of vLLM's silu_and_mul_nvfp4_quant, which its
+ * fuse_act_quant pass substitutes for silu_and_mul + scaled_fp4_quant
+ * (vllm 0.22 compilation/passes/fusion/act_quant_fusion.py:124-172); the
+ * reference turns that pass off (run_bench_tune.sh:24,31) so that its own
+ * quantizer runs unfused.
+ */
+int ssw_silu_and_mul_scalesweep_mse_nvfp4_quant_out(const void* input, int input_dtype,
+                                                    int64_t num_rows, int64_t n,
+                                                    const float* input_scale, uint8_t* output,
+                                                    uint8_t* output_scale,
+                                                    int is_sf_swizzled_layout, void* stream);
+
+/*
  * Plain round-to-nearest NVFP4 comparator: scale code = clamp(e4m3(amax/6),1,126),
  * codes = e2m1(v / scale), same layouts.  Stands in for vLLM's
  * scaled_fp4_quant.out that bench_kernel/custom.py:24-31 dispatches "cutlass"/"vllm" to.

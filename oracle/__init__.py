@@ -56,6 +56,9 @@ def lib():
         L.orc_e4m3_encode.argtypes = [ctypes.c_float]
         L.orc_e4m3_decode.restype = ctypes.c_float
         L.orc_e4m3_decode.argtypes = [ctypes.c_uint8]
+        L.orc_silu_mul.restype = ctypes.c_int
+        L.orc_silu_mul.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
+                                   ctypes.c_void_p, ctypes.c_int]
         _lib = L
     return _lib
 
@@ -89,6 +92,27 @@ def quantize(bits: np.ndarray, gsi: float, *, dtype: str = "bf16", padded_n: int
     if rc != 0:
         raise ValueError("oracle rejected the shape")
     return codes, scales
+
+
+def silu_mul(bits: np.ndarray, dtype: str = "bf16", nthreads: int = 0) -> np.ndarray:
+    """vLLM's silu_and_mul on a [m, 2n] bf16/f16 tensor given as uint16 bits:
+    returns the [m, n] bits of RN(RN(silu(gate)) * up) (``orc_silu_mul``)."""
+    bits = np.ascontiguousarray(bits, dtype=np.uint16)
+    m, n2 = bits.shape
+    if n2 % 2:
+        raise ValueError("the last dimension must be even (gate, then up)")
+    out = np.empty((m, n2 // 2), np.uint16)
+    if lib().orc_silu_mul(bits.ctypes.data, _DTYPES[dtype], m, n2 // 2, out.ctypes.data,
+                          int(nthreads)) != 0:
+        raise ValueError("oracle rejected the shape")
+    return out
+
+
+def silu_mul_quantize(bits: np.ndarray, gsi: float, *, dtype: str = "bf16",
+                      swizzled: bool = True) -> tuple[np.ndarray, np.ndarray]:
+    """The fused SiLU-and-mul quantizer: ``quantize(silu_mul(bits))`` with the
+    scalesweep_mse window."""
+    return quantize(silu_mul(bits, dtype), gsi, dtype=dtype, swizzled=swizzled)
 
 
 def absmax(bits: np.ndarray, dtype: str = "bf16", nthreads: int = 0) -> float:

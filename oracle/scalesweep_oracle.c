@@ -22,6 +22,10 @@
  *       (+ "scalesweep128")        rounded squares accumulated with the importance
  *                                  weights the host passes (all ones, :314)
  *   RTN comparator                 single candidate at the window's base code
+ *   SiLU-and-mul producer          vLLM's silu_and_mul (vllm 0.22 torch.ops._C.silu_and_mul,
+ *                                  model_executor/layers/activation.py:117-147): silu in
+ *                                  binary32 rounded to the input type, times up, rounded
+ *                                  once; pinned to tests/golden/silu_golden.npz
  *
  * Hardware semantics the reference's inline PTX and Triton casts rely on,
  * pinned on a B200 with a probe and restated here:
@@ -308,6 +312,75 @@ int orc_dequantize(const uint8_t* codes, const uint8_t* scales, int64_t m, int64
       int64_t blk = c / 16;
       int64_t off = swizzled ? orc_swizzled_offset(r, blk, bpc_pad) : r * bpc + blk;
       out[r * n + c] = e2m1_decode(nib) * e4m3_decode(scales[off]);
+    }
+  return 0;
+}
+
+/* ---- SiLU-and-mul ------------------------------------------------------ */
+
+/* Nearest-even rounding of x to a binary format with `mbits` fraction bits,
+   minimum normal exponent `emin` and largest finite value `maxval`
+   (subnormals included; overflow to infinity). */
+static double round_to_format(double x, int mbits, int emin, double maxval) {
+  if (isnan(x) || isinf(x) || x == 0.0) return x;
+  int e;
+  frexp(x, &e); /* |x| = f * 2^e with f in [0.5, 1): leading bit 2^(e-1) */
+  int lead = e - 1 < emin ? emin : e - 1;
+  double q = ldexp(nearbyint(ldexp(x, mbits - lead)), lead - mbits);
+  if (fabs(q) > maxval) return copysign(INFINITY, x);
+  return q;
+}
+
+static double round_to_dtype(double x, int dtype) {
+  return dtype == ORC_F16 ? round_to_format(x, 10, -14, 65504.0)
+                          : round_to_format(x, 7, -126, ldexp(255.0, 120));
+}
+
+/* Bits of a value that is exactly representable in the 16-bit type. */
+static uint16_t encode_dtype(double q, int dtype) {
+  if (dtype == ORC_BF16) {
+    if (isnan(q)) return 0x7FC0;
+    return (uint16_t)(f2u((float)q) >> 16);
+  }
+  uint16_t sign = signbit(q) ? 0x8000 : 0;
+  double a = fabs(q);
+  if (isnan(q)) return 0x7E00;
+  if (isinf(q)) return (uint16_t)(sign | 0x7C00);
+  if (a < ldexp(1.0, -14)) return (uint16_t)(sign | (uint16_t)ldexp(a, 24));
+  int e;
+  double f = frexp(a, &e); /* a = f * 2^e, f in [0.5, 1) */
+  uint32_t mant = (uint32_t)ldexp(f * 2.0 - 1.0, 10);
+  return (uint16_t)(sign | ((uint32_t)(e - 1 + 15) << 10) | mant);
+}
+
+/* silu(x) = x / (1 + e^-x) in binary32; e^-x is the correctly rounded float.
+   The device's expf gives the same silu after rounding to bf16 or f16 for
+   every input of those types (tests/golden/silu_golden.npz). */
+static float silu_f32(float x) {
+  float e = (float)exp(-(double)x);
+  return x / (1.0f + e);
+}
+
+/*
+ * input : [m, 2n] bf16/f16 bits (gate = columns 0..n-1, up = n..2n-1)
+ * out   : [m, n]  bits of RN(RN(silu(gate)) * up) in the same type
+ */
+int orc_silu_mul(const uint16_t* input, int dtype, int64_t m, int64_t n, uint16_t* out,
+                 int nthreads) {
+  if (m < 0 || n < 0) return -1;
+#ifdef _OPENMP
+  if (nthreads <= 0) nthreads = omp_get_max_threads();
+#pragma omp parallel for num_threads(nthreads) schedule(static)
+#else
+  (void)nthreads;
+#endif
+  for (int64_t r = 0; r < m; ++r)
+    for (int64_t c = 0; c < n; ++c) {
+      float g = load_elem(input + r * 2 * n + c, dtype);
+      float u = load_elem(input + r * 2 * n + n + c, dtype);
+      double s = round_to_dtype((double)silu_f32(g), dtype);
+      double h = round_to_dtype(s * (double)u, dtype); /* exact product, rounded once */
+      out[r * n + c] = encode_dtype(h, dtype);
     }
   return 0;
 }

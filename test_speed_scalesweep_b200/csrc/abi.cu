@@ -49,9 +49,12 @@ int device_sms(int* sms) {
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// silu_mul: `input` is [num_rows, 2n] and the quantized values are
+// silu(input[:, :n]) * input[:, n:] (scalesweep_mse window only).
 int quant_out(const char* name, int variant, int mode, const void* input, int input_dtype,
               int64_t num_rows, int64_t n, int64_t physical_n, const float* input_scale,
-              uint8_t* output, uint8_t* output_scale, int swizzled, void* stream) {
+              uint8_t* output, uint8_t* output_scale, int swizzled, void* stream,
+              bool silu_mul = false) {
   g_last_error.clear();
   if (input_dtype != SSW_DTYPE_BF16 && input_dtype != SSW_DTYPE_F16)
     return fail(SSW_ERR_INVALID_ARGUMENT, "%s: input dtype must be bf16 or f16 (got %d)", name,
@@ -95,15 +98,22 @@ int quant_out(const char* name, int variant, int mode, const void* input, int in
   ssw::make_divider(p.bpc_out, &p.div_magic, &p.div_shift);
   p.swizzled = swizzled ? 1 : 0;
   p.scale_word_stores = (bpc_out % 4 == 0) && aligned(output_scale, 4);
+  p.silu_row_elems = silu_mul ? 2 * (uint64_t)n : 0;
   const bool vec = aligned(input, 32) && aligned(output, 8);
+  if (silu_mul && !vec)
+    return fail(SSW_ERR_INVALID_ARGUMENT,
+                "%s: input must be 32-byte aligned and output 8-byte aligned", name);
 
   int sms = 0;
   int st = device_sms(&sms);
   if (st != SSW_OK) return st;
   const int lanes = ssw::quant_lanes_per_block(nblocks, sms, mode, vec);
   const int grid = ssw::quant_grid_size(nblocks, sms, lanes);
-  cudaError_t e = ssw::launch_quant(p, variant, mode, input_dtype, vec, lanes, grid,
-                                    static_cast<cudaStream_t>(stream));
+  cudaError_t e =
+      silu_mul ? ssw::launch_silu_mul_quant(p, input_dtype, lanes, grid,
+                                            static_cast<cudaStream_t>(stream))
+               : ssw::launch_quant(p, variant, mode, input_dtype, vec, lanes, grid,
+                                   static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, name);
   return SSW_OK;
 }
@@ -206,6 +216,47 @@ int ssw_scalesweep128_nvfp4_quant_out(const void* input, int input_dtype, int64_
   return quant_out("scalesweep128_nvfp4_quant_out", ssw::kVariantWeighted, ssw::kModeFullRange,
                    input, input_dtype, num_rows, n, physical_n, input_scale, output, output_scale,
                    is_sf_swizzled_layout, stream);
+}
+
+int ssw_silu_and_mul(const void* input, int input_dtype, int64_t num_rows, int64_t n,
+                     void* output, void* stream) {
+  g_last_error.clear();
+  const char* name = "silu_and_mul";
+  if (input_dtype != SSW_DTYPE_BF16 && input_dtype != SSW_DTYPE_F16)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: input dtype must be bf16 or f16 (got %d)", name,
+                input_dtype);
+  if (num_rows < 0 || n < 0) return fail(SSW_ERR_INVALID_ARGUMENT, "%s: negative size", name);
+  if (n % 16)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: n must be a multiple of 16 (got %lld)", name,
+                (long long)n);
+  const uint64_t chunks = (uint64_t)num_rows * (uint64_t)(n / 16);
+  if (chunks == 0) return SSW_OK;
+  if (chunks >= (1ull << 32))
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: %llu 16-element chunks exceed the 2^32 per-call limit",
+                name, (unsigned long long)chunks);
+  if (!input || !output) return fail(SSW_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (!aligned(input, 32) || !aligned(output, 16))
+    return fail(SSW_ERR_INVALID_ARGUMENT,
+                "%s: input must be 32-byte aligned and output 16-byte aligned", name);
+  int sms = 0;
+  int st = device_sms(&sms);
+  if (st != SSW_OK) return st;
+  cudaError_t e = ssw::launch_silu_mul(static_cast<const uint16_t*>(input),
+                                       static_cast<uint16_t*>(output), (uint64_t)num_rows,
+                                       (uint32_t)n, input_dtype, sms,
+                                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, name);
+  return SSW_OK;
+}
+
+int ssw_silu_and_mul_scalesweep_mse_nvfp4_quant_out(const void* input, int input_dtype,
+                                                    int64_t num_rows, int64_t n,
+                                                    const float* input_scale, uint8_t* output,
+                                                    uint8_t* output_scale,
+                                                    int is_sf_swizzled_layout, void* stream) {
+  return quant_out("silu_and_mul_scalesweep_mse_nvfp4_quant_out", ssw::kVariantMse,
+                   ssw::kModeWindow, input, input_dtype, num_rows, n, n, input_scale, output,
+                   output_scale, is_sf_swizzled_layout, stream, /*silu_mul=*/true);
 }
 
 int ssw_rtn_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows, int64_t n,

@@ -20,6 +20,8 @@
 //                 square and sum rounded (importance weights of 1;
 //                 bench_kernel/scalesweep_nvfp4_utils.py:40-149, :314)
 #include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "ptx.cuh"
@@ -140,6 +142,40 @@ __device__ __forceinline__ float sse_one(const uint64_t (&vp)[8], float inv) {
   }
 }
 
+// vLLM's silu_and_mul on a word of two 16-bit values: silu(g) = g / (1 + e^-g)
+// in binary32 (expf, IEEE division), rounded to the input type, then times
+// the up value in that type (one rounding of the exact product), as
+// torch.ops._C.silu_and_mul computes it (vllm 0.22, registered for
+// model_executor/layers/activation.py:117-147).
+//
+// bf16 takes a cheaper binary32 silu that rounds to the same bf16 for every
+// one of the 65536 bf16 inputs (checked exhaustively on B200 against vLLM):
+// __expf and the approximate division __fdividef, except below -64, where
+// 1 + e^-g can exceed 2^126 and __fdividef returns 0; there the IEEE
+// division.  f16 keeps expf and IEEE division: the cheaper forms differ from
+// vLLM on one or two f16 inputs.
+__device__ __forceinline__ float silu_bf16_exact(float g) {
+  const float d = 1.0f + __expf(-g);
+  return g < -64.0f ? g / d : __fdividef(g, d);
+}
+
+template <int kDType>
+__device__ __forceinline__ uint32_t silu_mul2(uint32_t g, uint32_t u) {
+  if constexpr (kDType == kDTypeBF16) {
+    const __nv_bfloat162 gb = *reinterpret_cast<const __nv_bfloat162*>(&g);
+    const __nv_bfloat162 s = __floats2bfloat162_rn(silu_bf16_exact(__low2float(gb)),
+                                                   silu_bf16_exact(__high2float(gb)));
+    const __nv_bfloat162 h = __hmul2(s, *reinterpret_cast<const __nv_bfloat162*>(&u));
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __half2 gh = *reinterpret_cast<const __half2*>(&g);
+    const float g0 = __low2float(gh), g1 = __high2float(gh);
+    const __half2 s = __floats2half2_rn(g0 / (1.0f + expf(-g0)), g1 / (1.0f + expf(-g1)));
+    const __half2 h = __hmul2(s, *reinterpret_cast<const __half2*>(&u));
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
 __device__ __forceinline__ void consider(float mse, int raw, float& best, int& best_raw) {
   // strict '<': NaN never wins and ties keep the earlier (lower-index) candidate
   if (mse < best) {
@@ -212,10 +248,13 @@ __device__ __forceinline__ void merge_best(float& best, int& bi, float ob, int o
 // underfilled (decode-sized inputs): each sweeps the window candidates
 // i = sub, sub + kLanes, ... and the lanes merge their winners.  kLanes = 1 is
 // the throughput configuration: one lane per block, all 11 candidates.
-template <int kVariant, int kMode, int kDType, bool kVec, int kLanes>
+// kSiluMul: the block's 16 values are h = silu(gate) * up, formed from the
+// gate and up halves of a [rows, 2n] input (silu_mul2) instead of loaded.
+template <int kVariant, int kMode, int kDType, bool kVec, int kLanes, bool kSiluMul = false>
 __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantParams p) {
   static_assert(kLanes == 1 || (kMode == kModeWindow && (kLanes == 2 || kLanes == 4)),
                 "lane sharing applies to the 11-candidate window only");
+  static_assert(!kSiluMul || kVec, "the SiLU-and-mul input is read with vector loads");
   constexpr int kBlocksPerWarp = 32 / kLanes;
   // tab  : reciprocal and square of the E4M3 scale of every code 0..127
   //        (code 0 -> 1/0 = inf, used when no candidate wins)
@@ -263,13 +302,22 @@ __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantP
     // ---- load (bench_kernel/scalesweep_mse_nvfp4_utils.py:232-270)
     uint32_t w[8];
     if (has_data) {
-      const uint16_t* src = p.input + ((uint64_t)row * bpc_in + col) * 16;
-      if constexpr (kVec) {
-        ld_block_v8(src, w);
-      } else {
+      if constexpr (kSiluMul) {
+        const uint16_t* gate = p.input + (uint64_t)row * p.silu_row_elems + (uint64_t)col * 16;
+        uint32_t g[8], u[8];
+        ld_block_v8(gate, g);
+        ld_block_v8(gate + (uint64_t)bpc_in * 16, u);
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          w[j] = (uint32_t)__ldg(src + 2 * j) | ((uint32_t)__ldg(src + 2 * j + 1) << 16);
+        for (int j = 0; j < 8; ++j) w[j] = silu_mul2<kDType>(g[j], u[j]);
+      } else {
+        const uint16_t* src = p.input + ((uint64_t)row * bpc_in + col) * 16;
+        if constexpr (kVec) {
+          ld_block_v8(src, w);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            w[j] = (uint32_t)__ldg(src + 2 * j) | ((uint32_t)__ldg(src + 2 * j + 1) << 16);
+        }
       }
     } else {
 #pragma unroll
@@ -411,10 +459,40 @@ __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantP
   }
 }
 
-template <int kVariant, int kMode, int kDType, bool kVec, int kLanes>
+template <int kVariant, int kMode, int kDType, bool kVec, int kLanes, bool kSiluMul = false>
 cudaError_t launch_one(const QuantParams& p, int grid, cudaStream_t stream) {
-  quant_kernel<kVariant, kMode, kDType, kVec, kLanes><<<grid, kThreads, 0, stream>>>(p);
+  quant_kernel<kVariant, kMode, kDType, kVec, kLanes, kSiluMul><<<grid, kThreads, 0, stream>>>(p);
   return cudaGetLastError();
+}
+
+template <int kDType>
+cudaError_t launch_silu_lanes(const QuantParams& p, int lanes, int grid, cudaStream_t s) {
+  if (lanes == 4) return launch_one<kVariantMse, kModeWindow, kDType, true, 4, true>(p, grid, s);
+  if (lanes == 2) return launch_one<kVariantMse, kModeWindow, kDType, true, 2, true>(p, grid, s);
+  if (lanes != 1) return cudaErrorInvalidValue;
+  return launch_one<kVariantMse, kModeWindow, kDType, true, 1, true>(p, grid, s);
+}
+
+// SiLU-and-mul alone: thread t handles 16-element chunks t, t + stride, ...
+// (two 32-byte loads, one 32-byte store each).
+template <int kDType>
+__global__ void __launch_bounds__(kThreads) silu_mul_kernel(const uint16_t* __restrict__ in,
+                                                            uint16_t* __restrict__ out,
+                                                            uint64_t nchunks, uint32_t cpr,
+                                                            uint32_t magic, uint32_t shift) {
+  const uint64_t stride = (uint64_t)gridDim.x * kThreads;
+  for (uint64_t c = (uint64_t)blockIdx.x * kThreads + threadIdx.x; c < nchunks; c += stride) {
+    const uint32_t row = div_bpc((uint32_t)c, magic, shift), col = (uint32_t)c - row * cpr;
+    const uint16_t* gate = in + (uint64_t)row * cpr * 32 + (uint64_t)col * 16;
+    uint32_t g[8], u[8], h[8];
+    ld_block_v8(gate, g);
+    ld_block_v8(gate + (uint64_t)cpr * 16, u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = silu_mul2<kDType>(g[j], u[j]);
+    uint4* dst = reinterpret_cast<uint4*>(out + c * 16);
+    dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+    dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+  }
 }
 
 template <int kVariant, int kMode, int kDType>
@@ -436,6 +514,31 @@ cudaError_t launch_dtype(const QuantParams& p, int dtype, bool vec, int lanes, i
 }
 
 }  // namespace
+
+cudaError_t launch_silu_mul_quant(const QuantParams& p, int dtype, int lanes, int grid,
+                                  cudaStream_t stream) {
+  if (dtype == kDTypeBF16) return launch_silu_lanes<kDTypeBF16>(p, lanes, grid, stream);
+  return launch_silu_lanes<kDTypeF16>(p, lanes, grid, stream);
+}
+
+cudaError_t launch_silu_mul(const uint16_t* input, uint16_t* output, uint64_t rows, uint32_t n,
+                            int dtype, int device_sms, cudaStream_t stream) {
+  const uint32_t cpr = n / 16;  // chunks per row
+  const uint64_t nchunks = rows * cpr;
+  if (nchunks == 0) return cudaSuccess;
+  uint32_t magic = 0, shift = 0;
+  make_divider(cpr, &magic, &shift);
+  const uint64_t want = (nchunks + kThreads - 1) / kThreads;
+  const uint64_t cap = (uint64_t)device_sms * 8;
+  const int grid = (int)(want < cap ? want : cap);
+  if (dtype == kDTypeBF16)
+    silu_mul_kernel<kDTypeBF16><<<grid, kThreads, 0, stream>>>(input, output, nchunks, cpr, magic,
+                                                              shift);
+  else
+    silu_mul_kernel<kDTypeF16><<<grid, kThreads, 0, stream>>>(input, output, nchunks, cpr, magic,
+                                                             shift);
+  return cudaGetLastError();
+}
 
 void make_divider(uint32_t d, uint32_t* magic, uint32_t* shift) {
   uint32_t l = 0;

@@ -24,6 +24,7 @@ struct QuantParams {
   uint32_t div_shift;
   int swizzled;
   int scale_word_stores;      // bpc_out % 4 == 0 and output_scale 4-byte aligned
+  uint64_t silu_row_elems;    // SiLU-and-mul input only: elements per input row (2 * n)
 };
 
 // Lanes sharing one block (1, 2 or 4): more than 1 only for the 11-candidate
@@ -34,6 +35,14 @@ int quant_grid_size(uint64_t nblocks, int device_sms, int lanes);
 void make_divider(uint32_t d, uint32_t* magic, uint32_t* shift);
 cudaError_t launch_quant(const QuantParams& p, int variant, int mode, int dtype, bool vec,
                          int lanes, int grid, cudaStream_t stream);
+// The "scalesweep_mse" window quantizer on h = silu(gate) * up of an input
+// [rows, 2n] (gate = columns 0..n-1, up = n..2n-1), computed on the fly as
+// vLLM's silu_and_mul computes it.  Vector loads only (input 32-byte aligned).
+cudaError_t launch_silu_mul_quant(const QuantParams& p, int dtype, int lanes, int grid,
+                                  cudaStream_t stream);
+// The SiLU-and-mul alone: output [rows, n] = silu(input[:, :n]) * input[:, n:].
+cudaError_t launch_silu_mul(const uint16_t* input, uint16_t* output, uint64_t rows, uint32_t n,
+                            int dtype, int device_sms, cudaStream_t stream);
 
 // amax / global scale
 struct AmaxParams {

@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import torch
 
+from . import act_quant
 from . import scalesweep_mse_nvfp4_utils as mse
 from . import scalesweep_mse_reference_nvfp4_utils as mse_ref
 from . import scalesweep_nvfp4_utils as sweep
@@ -89,7 +90,51 @@ def _register(namespace: str, kind: str) -> None:
         lib.impl(name + ".out", out_variant, "CUDA")
         torch.library.register_fake(f"{namespace}::{name}", fake_functional, lib=lib)
         torch.library.register_fake(f"{namespace}::{name}.out", fake_out, lib=lib)
+    if namespace == NAMESPACE:
+        _register_act_quant(lib, namespace)
     _libs[namespace] = lib
+
+
+def _register_act_quant(lib: torch.library.Library, namespace: str) -> None:
+    """SiLU-and-mul and the fused SiLU-and-mul quantizer (act_quant.py).
+    ``silu_and_mul`` and ``silu_and_mul_nvfp4_quant`` take vLLM's schemas
+    (``torch.ops._C.silu_and_mul(out, input)``,
+    ``torch.ops._C.silu_and_mul_nvfp4_quant(result, result_block_scale, input,
+    input_global_scale)``), so a fusion pass can target them unchanged."""
+    fused = "silu_and_mul_scalesweep_mse_nvfp4_quant"
+    lib.define(fused + "(Tensor input, Tensor input_scale, bool is_sf_swizzled_layout=True) "
+               "-> (Tensor, Tensor)")
+    lib.define(fused + ".out(Tensor input, Tensor input_scale, bool is_sf_swizzled_layout=True, "
+               "*, Tensor(a!) output, Tensor(b!) output_scale) -> ()")
+    lib.define("silu_and_mul(Tensor(a!) out, Tensor input) -> ()")
+    lib.define("silu_and_mul_nvfp4_quant(Tensor(a!) result, Tensor(b!) result_block_scale, "
+               "Tensor input, Tensor input_global_scale) -> ()")
+
+    def fused_functional(input, input_scale, is_sf_swizzled_layout=True):
+        return act_quant.silu_and_mul_scalesweep_mse_nvfp4_quant(input, input_scale,
+                                                                 is_sf_swizzled_layout)
+
+    def fused_out(input, input_scale, is_sf_swizzled_layout=True, *, output, output_scale):
+        act_quant.silu_and_mul_scalesweep_mse_nvfp4_quant_out(
+            input, input_scale, is_sf_swizzled_layout, output=output, output_scale=output_scale)
+
+    def silu_mul(out, input):
+        act_quant.silu_and_mul(input, out)
+
+    def fake_fused(input, input_scale, is_sf_swizzled_layout=True):
+        return act_quant.alloc_outputs(input, is_sf_swizzled_layout)
+
+    def fake_none(*args, **kwargs):
+        return None
+
+    lib.impl(fused, fused_functional, "CUDA")
+    lib.impl(fused + ".out", fused_out, "CUDA")
+    lib.impl("silu_and_mul", silu_mul, "CUDA")
+    lib.impl("silu_and_mul_nvfp4_quant", act_quant.silu_and_mul_nvfp4_quant, "CUDA")
+    torch.library.register_fake(f"{namespace}::{fused}", fake_fused, lib=lib)
+    torch.library.register_fake(f"{namespace}::{fused}.out", fake_none, lib=lib)
+    torch.library.register_fake(f"{namespace}::silu_and_mul", fake_none, lib=lib)
+    torch.library.register_fake(f"{namespace}::silu_and_mul_nvfp4_quant", fake_none, lib=lib)
 
 
 def register() -> None:
