@@ -69,6 +69,9 @@ def parse_args():
                     help="only run the NVFP4 GEMM 4 times on one shape and exit (for ncu)")
     ap.add_argument("--profile-amax", default=None, metavar="MxK",
                     help="only run the fused amax + global-scale kernel 4 times and exit")
+    ap.add_argument("--profile-act", default=None, metavar="MxN",
+                    help="only run silu_and_mul and the fused SiLU-and-mul quantizer on a "
+                         "[M, 2N] input 4 times each and exit (for ncu)")
     return ap.parse_args()
 
 
@@ -711,6 +714,24 @@ def run_profile_amax(args):
     print(json.dumps({"profile_amax": [m, k]}))
 
 
+def run_profile_act(args):
+    import torch
+    from test_speed_scalesweep_b200 import act_quant
+    m, n = (int(v) for v in args.profile_act.lower().split("x"))
+    device = torch.device("cuda", 0)
+    x = make_shard(m, 2 * n, 17, device)
+    gsi = torch.tensor([FP8_MAX * 6.0 / 40.0], dtype=torch.float32, device=device)
+    h = torch.empty(m, n, dtype=x.dtype, device=device)
+    codes, scales = act_quant.alloc_outputs(x, True)
+    for _ in range(4):
+        act_quant.silu_and_mul(x, h)
+    for _ in range(4):
+        act_quant.silu_and_mul_scalesweep_mse_nvfp4_quant_out(x, gsi, True, output=codes,
+                                                              output_scale=scales)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_act": [m, n]}))
+
+
 def main():
     args = parse_args()
     if args.profile_case:
@@ -721,6 +742,9 @@ def main():
         return
     if args.profile_amax:
         run_profile_amax(args)
+        return
+    if args.profile_act:
+        run_profile_act(args)
         return
     if args.impl == "reference":
         run_reference(args)
