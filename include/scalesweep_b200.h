@@ -178,12 +178,15 @@ int ssw_global_scale_inv(const void* input, int input_dtype, int64_t numel, floa
  * swizzled layout (as written by the quantizers above, is_sf_swizzled_layout=1),
  * out: [m, n] bf16 row-major.  Requires k % 256 == 0 and n % 128 == 0
  * (SSW_ERR_UNSUPPORTED otherwise) and 16-byte aligned pointers.
- * When the output has too few 128x128 tiles to fill the GPU, the K loop is
- * split across CTAs; that needs `workspace` of
- * ssw_nvfp4_gemm_workspace_bytes(m, n, k) bytes (0 when no split is planned).
- * With a NULL or smaller workspace the GEMM runs unsplit.  Calls sharing a
- * workspace must not overlap.  `status` (optional, device int) becomes
- * non-zero if a bounded device wait gave up.
+ * When the output has too few 128x128 tiles to fill the GPU and K is long
+ * enough, the K loop is split across CTAs.  Splitting is opted into with a
+ * `workspace` of ssw_nvfp4_gemm_workspace_bytes(m, n, k) bytes (0 when no
+ * split is planned); with a NULL or smaller workspace the GEMM runs unsplit.
+ * Up to 8 splits of a tile run as one thread-block cluster and add their
+ * partials in distributed shared memory (the workspace is then unused);
+ * more splits add them through the workspace.  Calls sharing a workspace
+ * must not overlap.  `status` (optional, device int) becomes non-zero if a
+ * bounded device wait gave up.
  * Replaces vLLM's cutlass_scaled_fp4_mm, which the W4A4 linear layer calls
  * after activation quantization (vllm 0.22 model_executor/kernels/linear/
  * nvfp4/cutlass.py:64-71; the reference's fallback restatement is

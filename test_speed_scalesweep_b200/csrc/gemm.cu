@@ -56,6 +56,9 @@ constexpr int kMaxStages = 8;
 constexpr int kATile = kBM * kBKBytes;       // 16 KiB
 constexpr int kSFTile = 4 * 512;             // four 128x4 scale atoms (K block of 256)
 constexpr int kMaxSplits = 16;
+// Split-K reduces across a thread-block cluster (distributed shared memory)
+// up to this many splits (the portable cluster size), in global memory above.
+constexpr int kMaxClusterSplits = 8;
 // Split-K reduction: 128 rows x 32 fp32 columns of one split's partial
 // (16 KiB, contiguous in the partial layout) per ring slot.
 constexpr int kRedChunkBytes = kBM * 32 * 4;
@@ -252,6 +255,35 @@ __host__ __device__ __forceinline__ int a_box_rows(int64_t m) {
   return m < kBM ? (int)((m + 7) / 8 * 8) : kBM;
 }
 
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The shared::cluster address of the same shared-memory offset in CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// Four floats from another CTA's shared memory (shared::cluster address).
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void record_error(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
@@ -262,7 +294,8 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
                       const __grid_constant__ CUtensorMap map_b, const uint8_t* __restrict__ sfa,
                       const uint8_t* __restrict__ sfb, const float* __restrict__ alpha_ptr,
                       __nv_bfloat16* __restrict__ out, int m, int n, int k, int* status,
-                      float* __restrict__ partials, uint32_t* __restrict__ tile_tickets) {
+                      float* __restrict__ partials, uint32_t* __restrict__ tile_tickets,
+                      int cluster_red) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned stage ring (128B-swizzled tiles need 1024 B alignment)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -272,6 +305,8 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
   constexpr int kBN = BN, kBTile = T::kBTile, kStageBytes = T::kStageBytes;
   constexpr int kTmemCols = T::kTmemCols, kColSF = T::kColSF;
   constexpr int kRedSlots = T::kRedSlots;
+  constexpr int kPartStride = BN + 4;  // cluster split-K: fp32 partial row stride (floats)
+  static_assert(STAGES * T::kStageBytes >= kBM * kPartStride * 4, "partial fits the ring");
   Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kStageBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -432,6 +467,17 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
       uint32_t v[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
       if (!acc_ok || row >= m) continue;
+      if (splits > 1 && cluster_red) {
+        // this CTA's fp32 partial, row-major in its idle ring, rows padded by
+        // 4 floats so the 32 rows of a warp's float4 writes spread over the banks
+        float* prow = reinterpret_cast<float*>(smem) + (warp * 32 + lane) * kPartStride + c;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          *reinterpret_cast<float4*>(prow + 4 * q) =
+              make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                          __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+        continue;
+      }
       if (splits > 1) {
         // partial layout [column group of 4][row]: lanes (rows) of a warp write
         // 32 consecutive float4s
@@ -445,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
       }
       store_row32_bf16(out + (uint64_t)row * n + (uint64_t)n_tile * kBN + c, v, alpha);
     }
-    if (splits > 1) {
+    if (splits > 1 && !cluster_red) {
       // The last split to finish this tile adds every split's partial in split
       // order (deterministic) and writes bf16; nobody waits for another CTA.
       __threadfence();
@@ -592,6 +638,45 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
 
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
+  if (splits > 1 && cluster_red) {
+    // Split-K across the cluster (one CTA per K slice of this tile): every
+    // partial is staged; CTA r adds rows r, r + splits, ... of all partials
+    // in split order (deterministic) through distributed shared memory and
+    // writes bf16.  All threads of every CTA reach both cluster barriers.
+    cluster_sync();
+    const uint32_t rank = cluster_rank();
+    const int valid_rows = min(kBM, m - m_tile * kBM);
+    const int my_rows = valid_rows > (int)rank ? (valid_rows - (int)rank + splits - 1) / splits : 0;
+    constexpr int kCol4 = kBN / 4;
+    const uint32_t part_base = smem_u32(smem);
+    uint32_t bases[kMaxClusterSplits];
+#pragma unroll
+    for (int j = 0; j < kMaxClusterSplits; ++j)
+      bases[j] = j < splits ? cluster_addr(part_base, (uint32_t)j) : 0u;
+    const float alpha = __ldg(alpha_ptr);
+#pragma unroll 1
+    for (int it = threadIdx.x; it < my_rows * kCol4; it += kThreads) {
+      const int r = (int)rank + splits * (it / kCol4), c4 = it % kCol4;
+      const uint32_t off = (uint32_t)((r * kPartStride + c4 * 4) * 4);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < kMaxClusterSplits; ++j) {
+        if (j < splits) {  // split order, fixed
+          const float4 p = ld_dsmem_f4(bases[j] + off);
+          acc.x += p.x;
+          acc.y += p.y;
+          acc.z += p.z;
+          acc.w += p.w;
+        }
+      }
+      uint32_t lo, hi;
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(acc.y * alpha), "f"(acc.x * alpha));
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(acc.w * alpha), "f"(acc.z * alpha));
+      *reinterpret_cast<uint2*>(out + (uint64_t)(m_tile * kBM + r) * n +
+                                (uint64_t)n_tile * kBN + 4 * c4) = make_uint2(lo, hi);
+    }
+    cluster_sync();  // no CTA frees its partial while another still reads it
+  }
   if (warp == kWarpMma) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols));
@@ -675,25 +760,6 @@ struct __align__(8) PairBarriers {
   uint64_t acc_empty;
   uint32_t tmem_base;
 };
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile(
-      "barrier.cluster.arrive.release.aligned;\n\t"
-      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// The shared::cluster address of the same shared-memory offset in CTA `rank`.
-__device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
 
 __device__ __forceinline__ void mbar_arrive_local(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -1095,20 +1161,30 @@ size_t smem_bytes_pair() {
 }
 
 int choose_splits(int64_t m, int64_t n, int64_t k, int device_sms) {
-  // Split K only when the output tiles leave SMs idle and K is long enough
-  // that every split keeps at least 8 K blocks: a split CTA's fixed cost
-  // (prologue, pipeline fill, fp32 partial round trip) outweighs the gain on
-  // short K.  Measured on B200, splitting pays for tiles of at most 32 valid
-  // rows (cheap reduction) or for grids of very few tiles; a 64..128-row
-  // decode tile runs faster unsplit on the 64-wide deep-ring configuration.
+  // Split K only when the output tiles leave SMs idle, one wave of CTAs at
+  // most.  Up to kMaxClusterSplits splits of a tile form one CTA cluster and
+  // add their partials in distributed shared memory, so a split needs only 4
+  // K blocks of work.  More splits (very long K) reduce through global
+  // memory, whose round trip (~2 us to publish a partial) needs at least 8 K
+  // blocks per split.  Measured on B200 (128-wide tiles, 2 CTAs per SM):
+  // splitting pays for long K (>= 32 K blocks: M=128, K=14336 19.9 -> 12.1
+  // us) and for tiles of <= 32 rows from 16 K blocks in 4 or more splits
+  // (M=16, N=4096, K=4096: 7.8 -> 6.5 us); 2-3 splits of a 16-block K, or
+  // any split of a 128-row tile at K=4096, lost to the unsplit 64-wide tile.
   const int64_t tiles = (n / 128) * ((m + kBM - 1) / kBM);
   const int64_t kblocks = k / 256;
-  if (tiles >= device_sms || kblocks < 24) return 1;
-  if (m > 32 && tiles * 8 > device_sms) return 1;
-  int64_t s = device_sms / tiles;  // one wave: every split CTA resident at once
-  if (s > kblocks / 8) s = kblocks / 8;
-  if (s > kMaxSplits) s = kMaxSplits;
-  return s < 1 ? 1 : (int)s;
+  if (tiles >= device_sms) return 1;
+  const bool long_k = kblocks >= 32;
+  if (!long_k && !(m <= 32 && kblocks >= 16)) return 1;
+  int64_t s = device_sms / tiles;
+  if (s > kblocks / 4) s = kblocks / 4;
+  if (s > kMaxClusterSplits) {
+    s = s < kblocks / 8 ? s : kblocks / 8;
+    if (s > kMaxSplits) s = kMaxSplits;
+    if (s < kMaxClusterSplits) s = kMaxClusterSplits;
+  }
+  if (s < (long_k ? 2 : 4)) return 1;
+  return (int)s;
 }
 
 int choose_tile_n(int64_t m, int64_t n, int splits, int device_sms) {
@@ -1163,6 +1239,28 @@ cudaError_t launch_bn(const GemmArgs& g, int splits, cudaStream_t stream, const 
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const unsigned gx = (unsigned)(g.n / BN), gy = (unsigned)((g.m + kBM - 1) / kBM);
+  dim3 grid(gx, gy, (unsigned)splits);
+  if (splits > 1 && splits <= kMaxClusterSplits) {
+    // the K slices of a tile form one cluster and reduce in distributed shared memory
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem_bytes_for<BN, STAGES>();
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = (unsigned)splits;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, nvfp4_gemm_kernel<BN, STAGES>, map_a, map_b, g.sfa, g.sfb,
+                           g.alpha, static_cast<__nv_bfloat16*>(g.out), (int)g.m, (int)g.n,
+                           (int)g.k, g.status, static_cast<float*>(nullptr),
+                           static_cast<uint32_t*>(nullptr), 1);
+    if (e != cudaSuccess) *why = "cudaLaunchKernelEx (cluster split-K)";
+    return e;
+  }
   float* partials = nullptr;
   uint32_t* tickets = nullptr;
   if (splits > 1) {
@@ -1175,10 +1273,9 @@ cudaError_t launch_bn(const GemmArgs& g, int splits, cudaStream_t stream, const 
       return e;
     }
   }
-  dim3 grid(gx, gy, (unsigned)splits);
   nvfp4_gemm_kernel<BN, STAGES><<<grid, kThreads, smem_bytes_for<BN, STAGES>(), stream>>>(
       map_a, map_b, g.sfa, g.sfb, g.alpha, static_cast<__nv_bfloat16*>(g.out), (int)g.m, (int)g.n,
-      (int)g.k, g.status, partials, tickets);
+      (int)g.k, g.status, partials, tickets, 0);
   return cudaGetLastError();
 }
 

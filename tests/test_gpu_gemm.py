@@ -77,7 +77,11 @@ def test_gemm_matches_vllm_cutlass_fp4_gemm(lib, m, n, k):
     assert err <= TOL, err
 
 
-@pytest.mark.parametrize("m,n,k", [(16, 4096, 14336), (1, 128, 8192), (200, 384, 14336)])
+# cluster split-K (partials reduced in distributed shared memory): 4 splits,
+# 8 splits of one tile, 8 splits over two M tiles (the second 72 rows), 4
+# splits of a full 128-row tile; global-memory split-K: 10 splits at K=20480
+@pytest.mark.parametrize("m,n,k", [(16, 4096, 14336), (1, 128, 8192), (200, 384, 14336),
+                                   (128, 4096, 14336), (16, 1024, 20480)])
 def test_split_k_agrees_with_single_pass(lib, m, n, k):
     from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm
     assert lib.ssw_nvfp4_gemm_workspace_bytes(m, n, k) > 0  # these shapes are split
