@@ -346,7 +346,7 @@ def run_gemm_sweep(device, reps: int = 20):
     import torch
     from test_speed_scalesweep_b200 import custom, global_scale
     from test_speed_scalesweep_b200 import scalesweep_mse_nvfp4_utils as mse
-    from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm
+    from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm, scalesweep_nvfp4_linear
     try:
         import vllm._custom_ops as vops
         vllm_mm = vops.cutlass_scaled_fp4_mm if hasattr(torch.ops._C, "cutlass_scaled_fp4_mm") \
@@ -379,11 +379,15 @@ def run_gemm_sweep(device, reps: int = 20):
                 res["vllm_cutlass_gemm_us"] = round(vms * 1e3, 2)
                 res["vllm_cutlass_gemm_tflops"] = round(flops / (vms * 1e-3) / 1e12, 1)
 
-            def fused():
+            def two_calls():
                 ca, csa = mse.scalesweep_mse_nvfp4_quant_impl(x, a_gsi, True)
                 return cutlass_scaled_fp4_mm(ca, qb, csa, sb, alpha)
-            qms = graph_avg_ms(fused, reps, device)
+            qms = graph_avg_ms(two_calls, reps, device)
             res["quant_plus_gemm_us"] = round(qms * 1e3, 2)
+            # one call: the GEMM as a programmatic dependent launch of the quantizer
+            lms = graph_avg_ms(lambda: scalesweep_nvfp4_linear(x, a_gsi, qb, sb, alpha), reps,
+                               device)
+            res["quant_gemm_linear_us"] = round(lms * 1e3, 2)
             out[f"M{m}_K{k}_N{n}"] = res
             del x, qa, sa
         del qb, sb

@@ -199,6 +199,28 @@ int ssw_nvfp4_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
                    void* stream);
 
 /*
+ * A W4A4 linear layer's activation quantization and GEMM in one call:
+ * x [m, k] (bf16/f16) is quantized with the "scalesweep_mse" sweep
+ * (x_scale = its input_scale, as for ssw_scalesweep_mse_nvfp4_quant_out) into
+ * codes and swizzled scales in `workspace`, then
+ *   out[m, n] (bf16) = alpha[0] * (A (.) sfA) (B (.) sfB)^T
+ * as ssw_nvfp4_gemm computes it, bit for bit.  The GEMM is launched as a
+ * programmatic dependent of the quantizer: its prologue and its first
+ * stages of weight loads overlap the quantizer; it reads A only after the
+ * quantizer has finished.  workspace: 256-byte aligned, at least
+ * ssw_nvfp4_quant_gemm_workspace_bytes(m, n, k) bytes (A's codes and scales,
+ * then the GEMM's split-K scratch).  Same limits as ssw_nvfp4_gemm.
+ * Replaces the scaled_fp4_quant + cutlass_scaled_fp4_mm pair of vLLM's W4A4
+ * linear layer (vllm 0.22 model_executor/kernels/linear/nvfp4/cutlass.py:56-71),
+ * with the quantizer the reference hooks in there.
+ */
+int64_t ssw_nvfp4_quant_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k);
+int ssw_nvfp4_quant_gemm(const void* x, int x_dtype, const float* x_scale, const uint8_t* b,
+                         const uint8_t* b_scale, const float* alpha, void* out, int64_t m,
+                         int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
+                         int* status, void* stream);
+
+/*
  * ssw_global_scale_inv without any device memory from the caller.  No
  * counterpart in the reference: the reference computes the global scale with
  * torch, which allocates.  This entry point is for callers that own only the

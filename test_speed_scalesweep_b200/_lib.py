@@ -37,6 +37,9 @@ _SIGNATURES = {
     "ssw_global_scale_from_amax": (_int, [_c_p, _f32, _c_p, _c_p]),
     "ssw_global_scale_inv": (_int, [_c_p, _int, _i64, _f32, _c_p, _c_p, _c_p, _c_p]),
     "ssw_nvfp4_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64]),
+    "ssw_nvfp4_quant_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64]),
+    "ssw_nvfp4_quant_gemm": (_int, [_c_p, _int, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _i64,
+                                    _c_p, _i64, _c_p, _c_p]),
     "ssw_nvfp4_gemm": (_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _i64, _c_p, _i64,
                               _c_p, _c_p]),
     "ssw_global_scale_inv_noalloc_max_numel": (_i64, []),

@@ -147,6 +147,64 @@ int amax_common(const char* name, const void* input, int input_dtype, int64_t nu
   return SSW_OK;
 }
 
+int gemm_shape_check(const char* name, int64_t m, int64_t n, int64_t k) {
+  if (m < 0 || n <= 0 || k <= 0)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: bad sizes m=%lld n=%lld k=%lld", name,
+                (long long)m, (long long)n, (long long)k);
+  if (k % 256)
+    return fail(SSW_ERR_UNSUPPORTED, "%s: k must be a multiple of 256 (got %lld)", name,
+                (long long)k);
+  if (n % 128)
+    return fail(SSW_ERR_UNSUPPORTED, "%s: n must be a multiple of 128 (got %lld)", name,
+                (long long)n);
+  if (m >= (1ll << 31) || n >= (1ll << 31) || k >= (1ll << 31))
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: sizes must be below 2^31", name);
+  return SSW_OK;
+}
+
+int gemm_common(const char* name, const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
+                const uint8_t* b_scale, const float* alpha, void* out, int64_t m, int64_t n,
+                int64_t k, void* workspace, int64_t workspace_bytes, int* status, void* stream,
+                bool dependent_launch) {
+  int st = gemm_shape_check(name, m, n, k);
+  if (st != SSW_OK || m == 0) return st;
+  if (!a || !b || !a_scale || !b_scale || !alpha || !out)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(a_scale, 16) || !aligned(b_scale, 16) ||
+      !aligned(out, 16) || !aligned(alpha, 4) || (workspace && !aligned(workspace, 16)))
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: operands must be 16-byte aligned", name);
+  int sms = 0;
+  st = device_sms(&sms);
+  if (st != SSW_OK) return st;
+  int splits = ssw::gemm::choose_splits(m, n, k, sms);
+  // without (enough) workspace the GEMM runs unsplit
+  if (splits > 1 &&
+      (!workspace || workspace_bytes < (int64_t)ssw::gemm::workspace_bytes(m, n, k, splits)))
+    splits = 1;
+  ssw::gemm::GemmArgs g{a, b, a_scale, b_scale, alpha, out, m, n, k, status, workspace};
+  g.dependent_launch = dependent_launch;
+  const char* why = "launch";
+  cudaError_t e = ssw::gemm::launch(g, splits, static_cast<cudaStream_t>(stream), &why);
+  if (e != cudaSuccess) return cuda_fail(e, why);
+  return SSW_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Workspace of the fused quantize + GEMM call: A's codes, A's swizzled
+// scales, then the GEMM's split-K scratch.
+struct QuantGemmLayout {
+  size_t codes, scales, gemm, total;
+};
+QuantGemmLayout quant_gemm_layout(int64_t m, int64_t n, int64_t k, int sms) {
+  QuantGemmLayout l;
+  l.codes = align256((size_t)m * (size_t)(k / 2));
+  l.scales = align256((size_t)((m + 127) / 128 * 128) * (size_t)((k / 16 + 3) / 4 * 4));
+  l.gemm = ssw::gemm::workspace_bytes(m, n, k, ssw::gemm::choose_splits(m, n, k, sms));
+  l.total = l.codes + l.scales + l.gemm;
+  return l;
+}
+
 }  // namespace
 
 namespace ssw {
@@ -278,36 +336,39 @@ int ssw_nvfp4_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
                    int64_t k, void* workspace, int64_t workspace_bytes, int* status,
                    void* stream) {
   g_last_error.clear();
-  if (m < 0 || n <= 0 || k <= 0)
-    return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_gemm: bad sizes m=%lld n=%lld k=%lld",
-                (long long)m, (long long)n, (long long)k);
-  if (k % 256)
-    return fail(SSW_ERR_UNSUPPORTED, "nvfp4_gemm: k must be a multiple of 256 (got %lld)",
-                (long long)k);
-  if (n % 128)
-    return fail(SSW_ERR_UNSUPPORTED, "nvfp4_gemm: n must be a multiple of 128 (got %lld)",
-                (long long)n);
-  if (m >= (1ll << 31) || n >= (1ll << 31) || k >= (1ll << 31))
-    return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_gemm: sizes must be below 2^31");
-  if (m == 0) return SSW_OK;
-  if (!a || !b || !a_scale || !b_scale || !alpha || !out)
-    return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_gemm: null pointer");
-  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(a_scale, 16) || !aligned(b_scale, 16) ||
-      !aligned(out, 16) || !aligned(alpha, 4) || (workspace && !aligned(workspace, 16)))
-    return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_gemm: operands must be 16-byte aligned");
+  return gemm_common("nvfp4_gemm", a, b, a_scale, b_scale, alpha, out, m, n, k, workspace,
+                     workspace_bytes, status, stream, false);
+}
+
+int64_t ssw_nvfp4_quant_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   int sms = 0;
-  int st = device_sms(&sms);
+  if (m <= 0 || n <= 0 || k <= 0 || n % 128 || k % 256 || device_sms(&sms) != SSW_OK) return 0;
+  return (int64_t)quant_gemm_layout(m, n, k, sms).total;
+}
+
+int ssw_nvfp4_quant_gemm(const void* x, int x_dtype, const float* x_scale, const uint8_t* b,
+                         const uint8_t* b_scale, const float* alpha, void* out, int64_t m,
+                         int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
+                         int* status, void* stream) {
+  g_last_error.clear();
+  const char* name = "nvfp4_quant_gemm";
+  int st = gemm_shape_check(name, m, n, k);
+  if (st != SSW_OK || m == 0) return st;
+  int sms = 0;
+  st = device_sms(&sms);
   if (st != SSW_OK) return st;
-  int splits = ssw::gemm::choose_splits(m, n, k, sms);
-  // without (enough) workspace the GEMM runs unsplit
-  if (splits > 1 &&
-      (!workspace || workspace_bytes < (int64_t)ssw::gemm::workspace_bytes(m, n, k, splits)))
-    splits = 1;
-  ssw::gemm::GemmArgs g{a, b, a_scale, b_scale, alpha, out, m, n, k, status, workspace};
-  const char* why = "launch";
-  cudaError_t e = ssw::gemm::launch(g, splits, static_cast<cudaStream_t>(stream), &why);
-  if (e != cudaSuccess) return cuda_fail(e, why);
-  return SSW_OK;
+  const QuantGemmLayout lay = quant_gemm_layout(m, n, k, sms);
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < (int64_t)lay.total)
+    return fail(SSW_ERR_INVALID_ARGUMENT,
+                "%s: workspace must be 256-byte aligned and hold %llu bytes", name,
+                (unsigned long long)lay.total);
+  uint8_t* codes = static_cast<uint8_t*>(workspace);
+  uint8_t* scales = codes + lay.codes;
+  st = quant_out(name, ssw::kVariantMse, ssw::kModeWindow, x, x_dtype, m, k, k, x_scale, codes,
+                 scales, 1, stream);
+  if (st != SSW_OK) return st;
+  return gemm_common(name, codes, b, scales, b_scale, alpha, out, m, n, k, scales + lay.scales,
+                     (int64_t)lay.gemm, status, stream, /*dependent_launch=*/true);
 }
 
 int64_t ssw_absmax_workspace_bytes(void) { return 8; }

@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
                       const uint8_t* __restrict__ sfb, const float* __restrict__ alpha_ptr,
                       __nv_bfloat16* __restrict__ out, int m, int n, int k, int* status,
                       float* __restrict__ partials, uint32_t* __restrict__ tile_tickets,
-                      int cluster_red) {
+                      int cluster_red, int pdl_wait) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned stage ring (128B-swizzled tiles need 1024 B alignment)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -356,6 +356,28 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
   if (warp == kWarpProducer) {
     if (lane == 0) {
       // ---------------- producer
+      auto load_b = [&](int kb) {  // weights: never written by the previous kernel
+        const int s = kb % kStages, gkb = kb_begin + kb;
+        uint8_t* st = smem + s * kStageBytes;
+        tma_load_2d(st + kATile, &map_b, &bars->full[s], gkb * kBKBytes, n_tile * kBN);
+#pragma unroll
+        for (int slab = 0; slab < kSFBSlabs; ++slab)
+          bulk_load(st + kATile + kBTile + (1 + slab) * kSFTile,
+                    sfb_tile + slab * sf_row_stride + (uint64_t)gkb * kSFTile, kSFTile,
+                    &bars->full[s]);
+      };
+      // With a dependent launch (after the quantizer that writes A): arm the
+      // first stages and start their weight loads, then wait for the
+      // previous grid before the first read of A or its scales.
+      int early = 0;
+      if (pdl_wait) {
+        early = kblocks < kStages ? kblocks : kStages;
+        for (int kb = 0; kb < early; ++kb) {
+          mbar_expect_tx(&bars->full[kb], kStageBytes - (kBM - a_rows) * kBKBytes);
+          load_b(kb);
+        }
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+      }
       for (int kb = 0; kb < kblocks; ++kb) {
         const int s = kb % kStages;
         const uint32_t round = kb / kStages;
@@ -364,17 +386,14 @@ __global__ void __launch_bounds__(kThreads, Tile<BN, STAGES>::kCtasPerSm)
           break;
         }
         uint8_t* st = smem + s * kStageBytes;
-        mbar_expect_tx(&bars->full[s], kStageBytes - (kBM - a_rows) * kBKBytes);
+        if (kb >= early) {
+          mbar_expect_tx(&bars->full[s], kStageBytes - (kBM - a_rows) * kBKBytes);
+          load_b(kb);
+        }
         const int gkb = kb_begin + kb;  // global K block
         tma_load_2d(st, &map_a, &bars->full[s], gkb * kBKBytes, m_tile * kBM);
-        tma_load_2d(st + kATile, &map_b, &bars->full[s], gkb * kBKBytes, n_tile * kBN);
         bulk_load(st + kATile + kBTile, sfa_tile + (uint64_t)gkb * kSFTile, kSFTile,
                   &bars->full[s]);
-#pragma unroll
-        for (int slab = 0; slab < kSFBSlabs; ++slab)
-          bulk_load(st + kATile + kBTile + (1 + slab) * kSFTile,
-                    sfb_tile + slab * sf_row_stride + (uint64_t)gkb * kSFTile, kSFTile,
-                    &bars->full[s]);
       }
     }
     __syncwarp();
@@ -1240,30 +1259,11 @@ cudaError_t launch_bn(const GemmArgs& g, int splits, cudaStream_t stream, const 
   }
   const unsigned gx = (unsigned)(g.n / BN), gy = (unsigned)((g.m + kBM - 1) / kBM);
   dim3 grid(gx, gy, (unsigned)splits);
-  if (splits > 1 && splits <= kMaxClusterSplits) {
-    // the K slices of a tile form one cluster and reduce in distributed shared memory
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem_bytes_for<BN, STAGES>();
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = (unsigned)splits;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, nvfp4_gemm_kernel<BN, STAGES>, map_a, map_b, g.sfa, g.sfb,
-                           g.alpha, static_cast<__nv_bfloat16*>(g.out), (int)g.m, (int)g.n,
-                           (int)g.k, g.status, static_cast<float*>(nullptr),
-                           static_cast<uint32_t*>(nullptr), 1);
-    if (e != cudaSuccess) *why = "cudaLaunchKernelEx (cluster split-K)";
-    return e;
-  }
+  // the K slices of a tile form one cluster and reduce in distributed shared memory
+  const bool cluster = splits > 1 && splits <= kMaxClusterSplits;
   float* partials = nullptr;
   uint32_t* tickets = nullptr;
-  if (splits > 1) {
+  if (splits > 1 && !cluster) {
     partials = static_cast<float*>(g.workspace);
     tickets = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(g.workspace) +
                                           (size_t)splits * gx * gy * kBM * BN * sizeof(float));
@@ -1273,10 +1273,35 @@ cudaError_t launch_bn(const GemmArgs& g, int splits, cudaStream_t stream, const 
       return e;
     }
   }
-  nvfp4_gemm_kernel<BN, STAGES><<<grid, kThreads, smem_bytes_for<BN, STAGES>(), stream>>>(
-      map_a, map_b, g.sfa, g.sfb, g.alpha, static_cast<__nv_bfloat16*>(g.out), (int)g.m, (int)g.n,
-      (int)g.k, g.status, partials, tickets, 0);
-  return cudaGetLastError();
+  // a dependent launch directly after the kernel that writes A (the memset
+  // of the global-memory split path would stand between them)
+  const bool pdl = g.dependent_launch && (splits <= 1 || cluster);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem_bytes_for<BN, STAGES>();
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned na = 0;
+  if (cluster) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = (unsigned)splits;
+    ++na;
+  }
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  e = cudaLaunchKernelEx(&cfg, nvfp4_gemm_kernel<BN, STAGES>, map_a, map_b, g.sfa, g.sfb, g.alpha,
+                         static_cast<__nv_bfloat16*>(g.out), (int)g.m, (int)g.n, (int)g.k,
+                         g.status, partials, tickets, cluster ? 1 : 0, pdl ? 1 : 0);
+  if (e != cudaSuccess) *why = "cudaLaunchKernelEx";
+  return e;
 }
 
 cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, const char** why) {

@@ -19,6 +19,10 @@ struct GemmArgs {
   int64_t m, n, k;
   int* status;         // optional device int: set non-zero if a bounded wait gave up
   void* workspace;     // split-K partials + tile tickets (workspace_bytes(...)), 16B aligned
+  // Launched right after the kernel that writes a / sfa (programmatic
+  // dependent launch): the GEMM's prologue and first weight loads overlap
+  // that kernel's tail; A is read only after griddepcontrol.wait.
+  bool dependent_launch = false;
 };
 
 size_t smem_bytes();

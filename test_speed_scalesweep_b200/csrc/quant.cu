@@ -255,6 +255,10 @@ __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantP
   static_assert(kLanes == 1 || (kMode == kModeWindow && (kLanes == 2 || kLanes == 4)),
                 "lane sharing applies to the 11-candidate window only");
   static_assert(!kSiluMul || kVec, "the SiLU-and-mul input is read with vector loads");
+  // A GEMM launched as this grid's programmatic dependent may start its
+  // prologue now; it reads the codes only after griddepcontrol.wait, which
+  // waits for this whole grid to finish.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   constexpr int kBlocksPerWarp = 32 / kLanes;
   // tab  : reciprocal and square of the E4M3 scale of every code 0..127
   //        (code 0 -> 1/0 = inf, used when no candidate wins)

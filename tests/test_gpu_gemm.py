@@ -95,3 +95,26 @@ def test_split_k_agrees_with_single_pass(lib, m, n, k):
     assert torch.equal(split, split2)  # the split reduction order is fixed
     err = _rel_fro(split.float().cpu().numpy(), single.float().cpu().numpy().astype(np.float64))
     assert err <= TOL, err
+
+
+# One-call quantize + GEMM (programmatic dependent launch): unsplit 64-wide
+# decode tiles, cluster split-K, 128-wide tiles over two M tiles, the CTA-pair
+# kernel, and the global-memory split (launched without the dependency).
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (16, 6144, 4096), (16, 4096, 14336),
+                                   (200, 384, 1024), (2000, 2560, 512), (16, 1024, 20480)])
+def test_quant_gemm_linear_equals_quantize_then_gemm(lib, m, n, k):
+    from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm, scalesweep_nvfp4_linear
+    x, gsi_a, qa, sa = _quantized(m, k, 31 + m, 1.0, "scalesweep_mse")
+    _, gsi_b, qb, sb = _quantized(n, k, 32 + n, 0.02, "rtn")
+    alpha = (1.0 / (gsi_a * gsi_b)).reshape(1).float()
+    scale_a = gsi_a.reshape(1).float()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ref = cutlass_scaled_fp4_mm(qa, qb, sa, sb, alpha)
+    got = scalesweep_nvfp4_linear(x, scale_a, qb, sb, alpha, status=status)
+    # back to back, so each dependent GEMM follows its own quantizer
+    again = [scalesweep_nvfp4_linear(x, scale_a, qb, sb, alpha) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    assert torch.equal(got, ref)
+    for g in again:
+        assert torch.equal(g, ref)
