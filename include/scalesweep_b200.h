@@ -32,7 +32,7 @@ extern "C" {
 typedef enum {
   SSW_OK = 0,
   SSW_ERR_INVALID_ARGUMENT = 1, /* shape, dtype, alignment or pointer problem */
-  SSW_ERR_UNSUPPORTED = 2,      /* valid request this build does not implement */
+  SSW_ERR_UNSUPPORTED = 2,      /* valid request the library does not implement */
   SSW_ERR_CUDA = 3,             /* a CUDA runtime call failed (launch, attribute) */
   SSW_ERR_TIMEOUT = 4           /* a bounded device-side wait gave up */
 } ssw_status;
