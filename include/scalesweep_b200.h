@@ -225,8 +225,9 @@ int ssw_nvfp4_quant_gemm(const void* x, int x_dtype, const float* x_scale, const
  * counterpart in the reference: the reference computes the global scale with
  * torch, which allocates.  This entry point is for callers that own only the
  * input and output buffers -- a plugin inside an engine that plans all device
- * memory up front, or code running during a CUDA-graph capture that must not
- * allocate.  It allocates nothing and needs no workspace; its scratch is a
+ * memory up front and gives plugins no workspace, or a service that must keep
+ * its device memory fixed after start-up.  It allocates nothing and needs no
+ * workspace; its scratch is a
  * 32 KiB static __device__ array inside the library (held on every GPU that
  * loads the library until exit), one partial maximum per 32768-element chunk.
  * Limits and rules:

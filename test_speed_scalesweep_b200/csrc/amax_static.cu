@@ -3,10 +3,9 @@
 // ssw_global_scale_inv needs an 8-byte device workspace from its caller.
 // Some callers cannot provide one: they own only the buffers they hand in.
 // One example is a plugin inside an inference engine that plans every device
-// byte ahead of time and exposes no workspace to plugins.  Another is code
-// that runs while a CUDA graph is being captured under a runtime that forbids
-// new allocations there, because an allocation made during capture would
-// become part of the graph.
+// byte ahead of time and exposes no workspace to plugins.  Another is a
+// service that must keep its device memory footprint fixed once it has
+// started, so that it cannot run out of memory later.
 //
 // This file serves them with a variant of the same reduction whose scratch
 // is a file-scope __device__ array.  The array is created when the library is

@@ -2,8 +2,8 @@
 
 ``ssw_global_scale_inv_noalloc`` exists for callers that own only their input
 and output buffers and cannot hand the library a device workspace: a plugin in
-an engine that plans all device memory up front, or code running inside a
-CUDA-graph capture that must not allocate.  Its scratch is a static array
+an engine that plans all device memory up front, or a service that must keep
+its device memory fixed after start-up.  Its scratch is a static array
 inside the library, shared by every call.  This test calls it through the C
 ABI twice in a row, on different inputs, and requires the same bits as
 ``ssw_global_scale_inv`` (which uses a caller workspace) every time.  It runs
