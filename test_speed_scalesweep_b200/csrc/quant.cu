@@ -477,25 +477,39 @@ cudaError_t launch_silu_lanes(const QuantParams& p, int lanes, int grid, cudaStr
   return launch_one<kVariantMse, kModeWindow, kDType, true, 1, true>(p, grid, s);
 }
 
-// SiLU-and-mul alone: thread t handles 16-element chunks t, t + stride, ...
-// (two 32-byte loads, one 32-byte store each).
+// SiLU-and-mul alone: thread t handles 16-element chunks t, t + stride, ...,
+// two per loop trip with all four 32-byte loads issued before either chunk is
+// computed (one chunk per trip kept too few bytes in flight to stream HBM).
 template <int kDType>
 __global__ void __launch_bounds__(kThreads) silu_mul_kernel(const uint16_t* __restrict__ in,
                                                             uint16_t* __restrict__ out,
                                                             uint64_t nchunks, uint32_t cpr,
                                                             uint32_t magic, uint32_t shift) {
   const uint64_t stride = (uint64_t)gridDim.x * kThreads;
-  for (uint64_t c = (uint64_t)blockIdx.x * kThreads + threadIdx.x; c < nchunks; c += stride) {
-    const uint32_t row = div_bpc((uint32_t)c, magic, shift), col = (uint32_t)c - row * cpr;
-    const uint16_t* gate = in + (uint64_t)row * cpr * 32 + (uint64_t)col * 16;
-    uint32_t g[8], u[8], h[8];
-    ld_block_v8(gate, g);
-    ld_block_v8(gate + (uint64_t)cpr * 16, u);
+  for (uint64_t c0 = (uint64_t)blockIdx.x * kThreads + threadIdx.x; c0 < nchunks;
+       c0 += 2 * stride) {
+    const uint64_t c1 = c0 + stride;
+    const bool two = c1 < nchunks;
+    uint32_t g[2][8], u[2][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) h[j] = silu_mul2<kDType>(g[j], u[j]);
-    uint4* dst = reinterpret_cast<uint4*>(out + c * 16);
-    dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
-    dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+    for (int t = 0; t < 2; ++t) {
+      if (t == 1 && !two) break;
+      const uint64_t c = t ? c1 : c0;
+      const uint32_t row = div_bpc((uint32_t)c, magic, shift), col = (uint32_t)c - row * cpr;
+      const uint16_t* gate = in + (uint64_t)row * cpr * 32 + (uint64_t)col * 16;
+      ld_block_v8(gate, g[t]);
+      ld_block_v8(gate + (uint64_t)cpr * 16, u[t]);
+    }
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (t == 1 && !two) break;
+      uint32_t h[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) h[k] = silu_mul2<kDType>(g[t][k], u[t][k]);
+      uint4* dst = reinterpret_cast<uint4*>(out + (t ? c1 : c0) * 16);
+      dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+      dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+    }
   }
 }
 
