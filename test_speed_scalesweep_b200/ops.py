@@ -92,7 +92,27 @@ def _register(namespace: str, kind: str) -> None:
         torch.library.register_fake(f"{namespace}::{name}.out", fake_out, lib=lib)
     if namespace == NAMESPACE:
         _register_act_quant(lib, namespace)
+        _register_linear(lib, namespace)
     _libs[namespace] = lib
+
+
+def _register_linear(lib: torch.library.Library, namespace: str) -> None:
+    """The W4A4 linear layer in one op (``gemm.scalesweep_nvfp4_linear``):
+    scale-sweep quantization of ``x`` [M, K] and the NVFP4 GEMM against
+    ``weight`` [N, K/2], bf16 [M, N] out."""
+    from . import gemm
+
+    lib.define("scalesweep_nvfp4_linear(Tensor x, Tensor input_scale, Tensor weight, "
+               "Tensor weight_scale, Tensor alpha) -> Tensor")
+
+    def linear(x, input_scale, weight, weight_scale, alpha):
+        return gemm.scalesweep_nvfp4_linear(x, input_scale, weight, weight_scale, alpha)
+
+    def fake_linear(x, input_scale, weight, weight_scale, alpha):
+        return x.new_empty(tuple(x.shape[:-1]) + (weight.shape[0],), dtype=torch.bfloat16)
+
+    lib.impl("scalesweep_nvfp4_linear", linear, "CUDA")
+    torch.library.register_fake(f"{namespace}::scalesweep_nvfp4_linear", fake_linear, lib=lib)
 
 
 def _register_act_quant(lib: torch.library.Library, namespace: str) -> None:

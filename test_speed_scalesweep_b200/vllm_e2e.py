@@ -78,7 +78,11 @@ NVFP4_QUANT_CONFIG = {
     },
 }
 
-BACKENDS = ("scalesweep_mse", "scalesweep_mse_reference", "rtn", "cutlass")
+# "scalesweep_mse_linear": the whole W4A4 linear layer from this package --
+# scale-sweep quantization and this package's NVFP4 GEMM in one op
+# (install_linear_hook); the others swap only the activation quantizer.
+BACKENDS = ("scalesweep_mse", "scalesweep_mse_reference", "rtn", "cutlass",
+            "scalesweep_mse_linear")
 _OP_FOR_BACKEND = {"scalesweep_mse": "scalesweep_mse_nvfp4_quant",
                    "scalesweep_mse_reference": "scalesweep_mse_reference_nvfp4_quant",
                    "rtn": "rtn_nvfp4_quant"}
@@ -138,6 +142,50 @@ def install_act_quant_hook(backend: str) -> int:
     return rebound
 
 
+LINEAR_CALLS = {"ours": 0, "fallback": 0}
+
+
+def install_linear_hook() -> None:
+    """Route vLLM's W4A4 linear layer through ``scalesweep_nvfp4_linear``.
+
+    ``CutlassNvFp4LinearKernel.apply_weights`` (vllm 0.22
+    ``model_executor/kernels/linear/nvfp4/cutlass.py:45-77``) calls
+    ``scaled_fp4_quant`` and then ``cutlass_scaled_fp4_mm``.  The replacement
+    makes one call of the registered op
+    ``torch.ops.scalesweep_b200.scalesweep_nvfp4_linear``: this package's
+    quantizer, then its GEMM as a programmatic dependent launch.  Layers the
+    GEMM does not take (K-padded weights, K % 256, N % 128, non-bf16
+    activations) keep vLLM's method.
+    """
+    from . import ops  # noqa: F401  (registers torch.ops.scalesweep_b200.*)
+    from vllm.model_executor.kernels.linear.nvfp4.cutlass import CutlassNvFp4LinearKernel
+
+    original = CutlassNvFp4LinearKernel.apply_weights
+    if getattr(original, "_scalesweep_b200", False):
+        return
+
+    def apply_weights(self, layer, x, bias=None):
+        k = x.shape[-1]
+        n = layer.weight.shape[0]
+        if (getattr(layer, "weights_padding_cols", 0) or k % 256 or n % 128
+                or x.dtype != torch.bfloat16):
+            LINEAR_CALLS["fallback"] += 1
+            return original(self, layer, x, bias)
+        LINEAR_CALLS["ours"] += 1
+        out = torch.ops.scalesweep_b200.scalesweep_nvfp4_linear(
+            x.reshape(-1, k), layer.input_global_scale_inv, layer.weight, layer.weight_scale,
+            layer.alpha)
+        output_size = layer.output_size_per_partition
+        if n != output_size:
+            out = out[:, :output_size]
+        if bias is not None:
+            out = out + bias
+        return out.view(*x.shape[:-1], output_size)
+
+    apply_weights._scalesweep_b200 = True
+    CutlassNvFp4LinearKernel.apply_weights = apply_weights
+
+
 def init_random_nvfp4_weights(model: torch.nn.Module, act_amax: float = 16.0,
                               seed: int = 0) -> int:
     """Give every W4A4 linear layer seeded N(0, 0.02) weights, RTN-quantized to
@@ -176,7 +224,10 @@ def init_random_nvfp4_weights(model: torch.nn.Module, act_amax: float = 16.0,
 def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 0,
         gpu_memory_utilization: float = 0.85, enforce_eager: bool = False) -> dict:
     os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
-    rebound = install_act_quant_hook(backend)
+    linear_ours = backend == "scalesweep_mse_linear"
+    rebound = install_act_quant_hook("scalesweep_mse" if linear_ours else backend)
+    if linear_ours:
+        install_linear_hook()
     from vllm import LLM, SamplingParams
     from vllm.inputs import TokensPrompt
 
@@ -200,7 +251,8 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
                             detokenize=False, seed=seed)
     results = {"backend": backend, "input_len": input_len, "output_len": output_len,
                "quantized_layers": n_layers, "hook_rebound_names": rebound, "batch": {},
-               "linear_backend": "cutlass", "fusion": "off",
+               "linear_backend": ("scalesweep_b200 quantizer + GEMM (one op)" if linear_ours
+                                  else "vLLM CUTLASS"), "fusion": "off",
                "weights": "random N(0, 0.02), RTN-quantized to NVFP4 in-process",
                "prompts": "uniform-random token ids, ignore_eos"}
     warm = [TokensPrompt(prompt_token_ids=torch.randint(0, 128000, (input_len,),
@@ -222,6 +274,8 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
             "total_tok_s": round((n_out + bs * input_len) / dt, 2),
             "seconds": round(dt, 3), "output_tokens": n_out}
     results["hook_calls_during_compile_and_capture"] = HOOK_CALLS["count"]
+    if linear_ours:
+        results["linear_hook_calls"] = dict(LINEAR_CALLS)
     return results
 
 

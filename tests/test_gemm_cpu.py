@@ -77,3 +77,13 @@ def test_python_wrappers_reject_cpu_tensors_and_other_outputs():
         scalesweep_nvfp4_linear(x, torch.ones(1), b, s, alpha)
     with pytest.raises(ValueError, match="bf16 or f16"):
         scalesweep_nvfp4_linear(x.float(), torch.ones(1), b, s, alpha)
+
+
+def test_linear_op_traces_with_its_fake_shape():
+    from test_speed_scalesweep_b200 import ops  # noqa: F401
+    x = torch.empty(3, 5, 4096, dtype=torch.bfloat16, device="meta")
+    w = torch.empty(6144, 2048, dtype=torch.uint8, device="meta")
+    ws = torch.empty(6144, 256, dtype=torch.float8_e4m3fn, device="meta")
+    one = torch.empty(1, device="meta")
+    out = torch.ops.scalesweep_b200.scalesweep_nvfp4_linear(x, one, w, ws, one)
+    assert out.shape == (3, 5, 6144) and out.dtype == torch.bfloat16

@@ -114,7 +114,12 @@ def test_quant_gemm_linear_equals_quantize_then_gemm(lib, m, n, k):
     # back to back, so each dependent GEMM follows its own quantizer
     again = [scalesweep_nvfp4_linear(x, scale_a, qb, sb, alpha) for _ in range(3)]
     torch.cuda.synchronize()
+    # the registered op (what the vLLM linear hook calls)
+    from test_speed_scalesweep_b200 import ops  # noqa: F401
+    via_op = torch.ops.scalesweep_b200.scalesweep_nvfp4_linear(x, scale_a, qb, sb, alpha)
+    torch.cuda.synchronize()
     assert status.item() == 0
     assert torch.equal(got, ref)
+    assert torch.equal(via_op, ref)
     for g in again:
         assert torch.equal(g, ref)
