@@ -81,8 +81,11 @@ NVFP4_QUANT_CONFIG = {
 # "scalesweep_mse_linear": the whole W4A4 linear layer from this package --
 # scale-sweep quantization and this package's NVFP4 GEMM in one op
 # (install_linear_hook); the others swap only the activation quantizer.
+# "scalesweep_mse_fused_act": additionally, each MLP's SiLU-and-mul and the
+# down projection's activation quantizer run as one fused kernel
+# (install_fused_act_hook), with vLLM's GEMM.
 BACKENDS = ("scalesweep_mse", "scalesweep_mse_reference", "rtn", "cutlass",
-            "scalesweep_mse_linear")
+            "scalesweep_mse_linear", "scalesweep_mse_fused_act")
 _OP_FOR_BACKEND = {"scalesweep_mse": "scalesweep_mse_nvfp4_quant",
                    "scalesweep_mse_reference": "scalesweep_mse_reference_nvfp4_quant",
                    "rtn": "rtn_nvfp4_quant"}
@@ -186,6 +189,54 @@ def install_linear_hook() -> None:
     CutlassNvFp4LinearKernel.apply_weights = apply_weights
 
 
+MLP_CALLS = {"fused": 0, "fallback": 0}
+
+
+def install_fused_act_hook() -> None:
+    """Fuse each Llama MLP's SiLU-and-mul into the down projection's
+    activation quantizer.
+
+    ``LlamaMLP.forward`` (vllm 0.22 ``model_executor/models/llama.py:117-121``)
+    runs gate_up_proj, ``SiluAndMul`` and down_proj; down_proj quantizes the
+    bf16 ``silu(gate) * up`` it is given.  The replacement hands gate_up_proj's
+    output straight to ``silu_and_mul_scalesweep_mse_nvfp4_quant`` with
+    down_proj's activation global scale, then runs vLLM's
+    ``cutlass_scaled_fp4_mm`` with down_proj's weights: the role vLLM's
+    ``fuse_act_quant`` pass plays for its own quantizer.  Layers that are not
+    single-GPU NVFP4 W4A4 linears without weight padding keep the original
+    forward.
+    """
+    from . import ops  # noqa: F401  (registers torch.ops.scalesweep_b200.*)
+    import vllm._custom_ops as vllm_ops
+    from vllm.model_executor.models.llama import LlamaMLP
+
+    original = LlamaMLP.forward
+    if getattr(original, "_scalesweep_b200", False):
+        return
+
+    def forward(self, x):
+        down = self.down_proj
+        if (getattr(down, "tp_size", 1) != 1 or getattr(down, "weights_padding_cols", 0)
+                or not all(hasattr(down, a) for a in ("input_global_scale_inv",
+                                                        "weight_scale", "alpha"))
+                or down.weight.dtype != torch.uint8):
+            MLP_CALLS["fallback"] += 1
+            return original(self, x)
+        MLP_CALLS["fused"] += 1
+        gate_up, _ = self.gate_up_proj(x)
+        codes, scales = torch.ops.scalesweep_b200.silu_and_mul_scalesweep_mse_nvfp4_quant(
+            gate_up.reshape(-1, gate_up.shape[-1]), down.input_global_scale_inv, True)
+        out = vllm_ops.cutlass_scaled_fp4_mm(codes, down.weight, scales, down.weight_scale,
+                                             down.alpha, gate_up.dtype)
+        out = out[:, :down.output_size_per_partition]
+        if down.bias is not None:
+            out = out + down.bias
+        return out.view(*gate_up.shape[:-1], down.output_size_per_partition)
+
+    forward._scalesweep_b200 = True
+    LlamaMLP.forward = forward
+
+
 def init_random_nvfp4_weights(model: torch.nn.Module, act_amax: float = 16.0,
                               seed: int = 0) -> int:
     """Give every W4A4 linear layer seeded N(0, 0.02) weights, RTN-quantized to
@@ -225,9 +276,12 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
         gpu_memory_utilization: float = 0.85, enforce_eager: bool = False) -> dict:
     os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
     linear_ours = backend == "scalesweep_mse_linear"
-    rebound = install_act_quant_hook("scalesweep_mse" if linear_ours else backend)
+    fused_act = backend == "scalesweep_mse_fused_act"
+    rebound = install_act_quant_hook("scalesweep_mse" if (linear_ours or fused_act) else backend)
     if linear_ours:
         install_linear_hook()
+    if fused_act:
+        install_fused_act_hook()
     from vllm import LLM, SamplingParams
     from vllm.inputs import TokensPrompt
 
@@ -276,6 +330,9 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
     results["hook_calls_during_compile_and_capture"] = HOOK_CALLS["count"]
     if linear_ours:
         results["linear_hook_calls"] = dict(LINEAR_CALLS)
+    if fused_act:
+        results["mlp_hook_calls"] = dict(MLP_CALLS)
+        results["fusion"] = "SiLU-and-mul + scale-sweep quant fused (this package)"
     return results
 
 
