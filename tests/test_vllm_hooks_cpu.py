@@ -1,0 +1,68 @@
+"""The vLLM hooks' routing, without a GPU: with meta tensors this package's
+ops run their fake implementations, so the tests check which layers take the
+package's path, which fall back to vLLM's, and the shapes that come out."""
+import types
+
+import pytest
+import torch
+
+vllm_cutlass = pytest.importorskip("vllm.model_executor.kernels.linear.nvfp4.cutlass")
+vllm_llama = pytest.importorskip("vllm.model_executor.models.llama")
+
+from test_speed_scalesweep_b200 import vllm_e2e  # noqa: E402
+
+
+def _layer(n=6144, k=4096, padding=0):
+    meta = dict(device="meta")
+    return types.SimpleNamespace(
+        weight=torch.empty(n, k // 2, dtype=torch.uint8, **meta),
+        weight_scale=torch.empty(n, k // 16, dtype=torch.float8_e4m3fn, **meta),
+        alpha=torch.empty(1, **meta), input_global_scale_inv=torch.empty(1, **meta),
+        output_size_per_partition=n, weights_padding_cols=padding, bias=None, tp_size=1)
+
+
+def test_linear_hook_routes_supported_layers_and_falls_back(monkeypatch):
+    seen = []
+
+    def original(self, layer, x, bias=None):
+        seen.append(layer)
+        return "vllm"
+
+    monkeypatch.setattr(vllm_cutlass.CutlassNvFp4LinearKernel, "apply_weights", original)
+    monkeypatch.setattr(vllm_e2e, "LINEAR_CALLS", {"ours": 0, "fallback": 0})
+    vllm_e2e.install_linear_hook()
+    apply = vllm_cutlass.CutlassNvFp4LinearKernel.apply_weights
+    x = torch.empty(2, 5, 4096, dtype=torch.bfloat16, device="meta")
+    out = apply(None, _layer(), x)
+    assert out.shape == (2, 5, 6144) and out.dtype == torch.bfloat16
+    padded = _layer(padding=8)
+    assert apply(None, padded, x) == "vllm" and seen == [padded]
+    assert apply(None, _layer(), x.float()) == "vllm"            # not bf16
+    assert apply(None, _layer(n=6144 + 64), x) == "vllm"         # N % 128
+    assert vllm_e2e.LINEAR_CALLS == {"ours": 1, "fallback": 3}
+
+
+def test_fused_act_hook_feeds_gate_up_to_the_fused_quantizer(monkeypatch):
+    def original(self, x):
+        return "vllm"
+
+    monkeypatch.setattr(vllm_llama.LlamaMLP, "forward", original)
+    monkeypatch.setattr(vllm_e2e, "MLP_CALLS", {"fused": 0, "fallback": 0})
+    calls = {}
+
+    def fake_mm(a, b, sa, sb, alpha, dtype):
+        calls["a"], calls["sa"] = a.shape, sa.shape
+        return torch.empty(a.shape[0], b.shape[0], dtype=dtype, device="meta")
+
+    import vllm._custom_ops as vllm_ops
+    monkeypatch.setattr(vllm_ops, "cutlass_scaled_fp4_mm", fake_mm)
+    vllm_e2e.install_fused_act_hook()
+    down = _layer(n=4096, k=14336)
+    gate_up = torch.empty(7, 2 * 14336, dtype=torch.bfloat16, device="meta")
+    mlp = types.SimpleNamespace(gate_up_proj=lambda x: (gate_up, None), down_proj=down)
+    out = vllm_llama.LlamaMLP.forward(mlp, torch.empty(7, 4096, device="meta"))
+    assert out.shape == (7, 4096)
+    assert calls["a"] == (7, 14336 // 2) and calls["sa"] == (128, 14336 // 16)
+    down.tp_size = 2                                             # tensor parallel: vLLM's path
+    assert vllm_llama.LlamaMLP.forward(mlp, gate_up) == "vllm"
+    assert vllm_e2e.MLP_CALLS == {"fused": 1, "fallback": 1}
