@@ -72,6 +72,9 @@ def parse_args():
     ap.add_argument("--profile-act", default=None, metavar="MxN",
                     help="only run silu_and_mul and the fused SiLU-and-mul quantizer on a "
                          "[M, 2N] input 4 times each and exit (for ncu)")
+    ap.add_argument("--profile-norm", default=None, metavar="MxN",
+                    help="only run the RMSNorm-fused quantizer (plain, then with a residual) "
+                         "on an [M, N] input 4 times each and exit (for ncu)")
     return ap.parse_args()
 
 
@@ -334,6 +337,70 @@ def run_act_fusion_sweep(device, reps: int = 20):
         out[f"M{m}"] = {"unfused_us": round(u_ms * 1e3, 2), "silu_and_mul_us": round(s_ms * 1e3, 2),
                         "fused_us": round(f_ms * 1e3, 2), "speedup": round(u_ms / f_ms, 3)}
         del x, h
+    return out
+
+
+NORM_FUSION_M = (16, 128, 1024, 8192)
+NORM_FUSION_N = 4096  # Llama-3.1-8B hidden size: the qkv and gate_up projections' input
+
+
+def run_norm_fusion_sweep(device, reps: int = 20):
+    """RMSNorm + scalesweep_mse on [M, 4096] decoder-layer inputs: vLLM's
+    rms_norm / fused_add_rms_norm, then the quantizer on the bf16 result (the
+    reference's pipeline, fuse_norm_quant off), against the fused op (row
+    statistics, then the quantizer normalising while it loads).  Needs vLLM's
+    compiled ops for the unfused leg; the fused times are reported either way."""
+    import torch
+    from test_speed_scalesweep_b200 import norm_quant
+    from test_speed_scalesweep_b200 import scalesweep_mse_nvfp4_utils as mse
+    try:
+        import vllm._custom_ops  # noqa: F401
+        have_vllm = hasattr(torch.ops._C, "rms_norm")
+    except Exception:
+        have_vllm = False
+    n, eps = NORM_FUSION_N, 1e-5
+    out = {"n": n, "method": "per-launch time from one CUDA graph of 20 launches"}
+    gsi = torch.tensor([FP8_MAX * 6.0 / 40.0], dtype=torch.float32, device=device)
+    g = torch.Generator(device=device).manual_seed(n)
+    w = (1.0 + 0.3 * torch.randn(n, generator=g, device=device)).to(torch.bfloat16)
+    for m in NORM_FUSION_M:
+        x = make_shard(m, n, 29 + m, device)
+        res = make_shard(m, n, 31 + m, device)
+        h = torch.empty_like(x)
+        rstd = torch.empty(m, dtype=torch.float32, device=device)
+        codes, scales = norm_quant.alloc_outputs(x, True)
+        r = {}
+
+        def fused():
+            norm_quant.rms_norm_scalesweep_mse_nvfp4_quant_out(
+                x, w, eps, gsi, True, output=codes, output_scale=scales, rstd=rstd)
+
+        def fused_add():
+            norm_quant.rms_norm_scalesweep_mse_nvfp4_quant_out(
+                x, w, eps, gsi, True, output=codes, output_scale=scales, residual=res, rstd=rstd)
+
+        r["fused_us"] = round(graph_avg_ms(fused, reps, device) * 1e3, 2)
+        r["fused_add_us"] = round(graph_avg_ms(fused_add, reps, device) * 1e3, 2)
+        if have_vllm:
+            def unfused():
+                torch.ops._C.rms_norm(h, x, w, eps)
+                mse.scalesweep_mse_nvfp4_quant_out(h, gsi, True, output=codes,
+                                                   output_scale=scales)
+
+            def unfused_add():
+                torch.ops._C.fused_add_rms_norm(h, res, w, eps)
+                mse.scalesweep_mse_nvfp4_quant_out(h, gsi, True, output=codes,
+                                                   output_scale=scales)
+
+            h.copy_(x)
+            r["vllm_rms_norm_us"] = round(
+                graph_avg_ms(lambda: torch.ops._C.rms_norm(h, x, w, eps), reps, device) * 1e3, 2)
+            r["unfused_us"] = round(graph_avg_ms(unfused, reps, device) * 1e3, 2)
+            r["unfused_add_us"] = round(graph_avg_ms(unfused_add, reps, device) * 1e3, 2)
+            r["speedup"] = round(r["unfused_us"] / r["fused_us"], 3)
+            r["speedup_add"] = round(r["unfused_add_us"] / r["fused_add_us"], 3)
+        out[f"M{m}"] = r
+        del x, res, h
     return out
 
 
@@ -632,6 +699,7 @@ def run_ours(args):
     gemm_res = None
     quality = None
     act_fusion = None
+    norm_fusion = None
     if rank == 0 and world == 1:
         del x
         torch.cuda.empty_cache()
@@ -642,6 +710,7 @@ def run_ours(args):
         if not args.no_sweep:
             quality = run_quality(device)
             act_fusion = run_act_fusion_sweep(device)
+            norm_fusion = run_norm_fusion_sweep(device)
         if not args.no_cpu:
             cpu = cpu_sample_rate(args.rows)
 
@@ -668,6 +737,8 @@ def run_ours(args):
             line["gemm"] = gemm_res
         if act_fusion is not None:
             line["act_fusion"] = act_fusion
+        if norm_fusion is not None:
+            line["norm_fusion"] = norm_fusion
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -736,6 +807,24 @@ def run_profile_act(args):
     print(json.dumps({"profile_act": [m, n]}))
 
 
+def run_profile_norm(args):
+    import torch
+    from test_speed_scalesweep_b200 import norm_quant
+    m, n = (int(v) for v in args.profile_norm.lower().split("x"))
+    device = torch.device("cuda", 0)
+    x = make_shard(m, n, 29, device)
+    res = make_shard(m, n, 31, device)
+    w = torch.ones(n, dtype=torch.bfloat16, device=device)
+    gsi = torch.tensor([FP8_MAX * 6.0 / 40.0], dtype=torch.float32, device=device)
+    codes, scales = norm_quant.alloc_outputs(x, True)
+    for resid in (None, res):
+        for _ in range(4):
+            norm_quant.rms_norm_scalesweep_mse_nvfp4_quant_out(
+                x, w, 1e-5, gsi, True, output=codes, output_scale=scales, residual=resid)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_norm": [m, n]}))
+
+
 def main():
     args = parse_args()
     if args.profile_case:
@@ -749,6 +838,9 @@ def main():
         return
     if args.profile_act:
         run_profile_act(args)
+        return
+    if args.profile_norm:
+        run_profile_norm(args)
         return
     if args.impl == "reference":
         run_reference(args)

@@ -131,6 +131,30 @@ int ssw_silu_and_mul_scalesweep_mse_nvfp4_quant_out(const void* input, int input
                                                     int is_sf_swizzled_layout, void* stream);
 
 /*
+ * RMSNorm fused into the "scalesweep_mse" quantizer: the codes and scales
+ * ssw_scalesweep_mse_nvfp4_quant_out would write for vLLM's RMSNorm output,
+ * without writing that bf16 intermediate.  bf16 only; input [num_rows, n],
+ * weight [n], n % 16 == 0; no padding (physical_n = n).
+ *   residual == NULL : the normalised values are vLLM's rms_norm(input, weight, eps).
+ *   residual != NULL : vLLM's fused_add_rms_norm: residual <- bf16(input + residual)
+ *                      (in place), and the normalised values are rms_norm(residual).
+ * Bit for bit vLLM's result: its per-token block size (1024 threads below 256
+ * tokens, 256 from there), its vector and CUB reduction order, rsqrtf of the
+ * IEEE mean, and one rounding of x * r * w were matched on a B200.
+ * rstd_workspace: num_rows floats of device scratch (1/rms per row, left
+ * there).  input, residual and weight 32-byte aligned, output 8-byte.
+ * This is the role of vLLM's fuse_norm_quant pass (vllm 0.22
+ * config/compilation.py:121-123) for this quantizer; the reference turns that
+ * pass off (run_bench_tune.sh:24,31).
+ */
+int ssw_rms_norm_scalesweep_mse_nvfp4_quant_out(const void* input, void* residual,
+                                                const void* weight, float eps, int64_t num_rows,
+                                                int64_t n, const float* input_scale,
+                                                uint8_t* output, uint8_t* output_scale,
+                                                int is_sf_swizzled_layout, float* rstd_workspace,
+                                                void* stream);
+
+/*
  * Plain round-to-nearest NVFP4 comparator: scale code = clamp(e4m3(amax/6),1,126),
  * codes = e2m1(v / scale), same layouts.  Stands in for vLLM's
  * scaled_fp4_quant.out that bench_kernel/custom.py:24-31 dispatches "cutlass"/"vllm" to.

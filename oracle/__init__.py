@@ -59,6 +59,12 @@ def lib():
         L.orc_silu_mul.restype = ctypes.c_int
         L.orc_silu_mul.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
                                    ctypes.c_void_p, ctypes.c_int]
+        L.orc_rms_sumsq.restype = ctypes.c_int
+        L.orc_rms_sumsq.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                    ctypes.c_int64, ctypes.c_void_p]
+        L.orc_rms_apply.restype = ctypes.c_int
+        L.orc_rms_apply.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]
         _lib = L
     return _lib
 
@@ -113,6 +119,43 @@ def silu_mul_quantize(bits: np.ndarray, gsi: float, *, dtype: str = "bf16",
     """The fused SiLU-and-mul quantizer: ``quantize(silu_mul(bits))`` with the
     scalesweep_mse window."""
     return quantize(silu_mul(bits, dtype), gsi, dtype=dtype, swizzled=swizzled)
+
+
+def rms_sumsq(bits: np.ndarray, residual: np.ndarray | None = None):
+    """vLLM's RMSNorm sum of squares per row of a [m, n] bf16 tensor given as
+    uint16 bits (``orc_rms_sumsq``).  With ``residual`` (fused_add_rms_norm)
+    the rows summed are bf16(x + residual); returns (acc float32 [m], the
+    updated residual bits or None)."""
+    bits = np.ascontiguousarray(bits, dtype=np.uint16)
+    m, n = bits.shape
+    acc = np.empty(m, np.float32)
+    res = None if residual is None else np.array(residual, dtype=np.uint16, order="C", copy=True)
+    if lib().orc_rms_sumsq(bits.ctypes.data, 0 if res is None else res.ctypes.data, m, n,
+                           acc.ctypes.data) != 0:
+        raise ValueError("oracle rejected the shape")
+    return acc, res
+
+
+def rms_apply(bits: np.ndarray, weight: np.ndarray, rstd: np.ndarray) -> np.ndarray:
+    """RMSNorm's output bits bf16(RN(RN(x * rstd[row]) * weight)) (``orc_rms_apply``)."""
+    bits = np.ascontiguousarray(bits, dtype=np.uint16)
+    weight = np.ascontiguousarray(weight, dtype=np.uint16)
+    rstd = np.ascontiguousarray(rstd, dtype=np.float32)
+    m, n = bits.shape
+    if weight.shape != (n,) or rstd.shape != (m,):
+        raise ValueError("weight must be [n] and rstd [m]")
+    out = np.empty_like(bits)
+    if lib().orc_rms_apply(bits.ctypes.data, weight.ctypes.data, rstd.ctypes.data, m, n,
+                           out.ctypes.data) != 0:
+        raise ValueError("oracle rejected the shape")
+    return out
+
+
+def rms_rsqrt_bound(acc: np.ndarray, n: int, eps: float) -> np.ndarray:
+    """1/sqrt(RN(RN(acc / n) + eps)) in float64: the value the device's rsqrtf
+    approximates (to within 2 ulp, CUDA's stated bound)."""
+    mean = np.float32(acc) / np.float32(n)
+    return 1.0 / np.sqrt((mean + np.float32(eps)).astype(np.float64))
 
 
 def absmax(bits: np.ndarray, dtype: str = "bf16", nthreads: int = 0) -> float:

@@ -16,6 +16,7 @@
  *       round-down base            :347-351
  *       pairwise tree SSE          :91-143
  *       swizzle                    :18-41
+ *   RMSNorm front end              vLLM 0.22 rms_norm / fused_add_rms_norm (orc_rms_sumsq)
  *   global scale                   bench_kernel/test_kernel_latency.py:65-75
  *       ((fp8_max*6) / amax is torch's Tensor.__rdiv__ = reciprocal(amax) * scalar)
  *   weighted "scalesweep"          bench_kernel/scalesweep_nvfp4_utils.py:184-302
@@ -381,6 +382,84 @@ int orc_silu_mul(const uint16_t* input, int dtype, int64_t m, int64_t n, uint16_
       double s = round_to_dtype((double)silu_f32(g), dtype);
       double h = round_to_dtype(s * (double)u, dtype); /* exact product, rounded once */
       out[r * n + c] = encode_dtype(h, dtype);
+    }
+  return 0;
+}
+
+/*
+ * vLLM's RMSNorm (vllm 0.22 torch.ops._C.rms_norm and
+ * torch.ops._C.fused_add_rms_norm, the ops behind
+ * model_executor/layers/layernorm.py RMSNorm.forward_cuda), restated from the
+ * order of operations its kernels were matched to bit for bit on a B200
+ * (bf16, n % 8 == 0).  vLLM launches one block of T threads per row, T = 1024
+ * below 256 rows and 256 from there; thread t takes the 8-element vectors
+ * t, t + T, ...; a block reduction adds the T partials: in each warp of 32, a
+ * shuffle-down tree (offsets 1, 2, 4, 8, 16; lane i adds lane i + o while
+ * i + o < 32), then the warp sums in warp order.
+ *
+ * orc_rms_sumsq: acc[row] = that sum of squares.
+ *   residual == NULL (rms_norm): each thread chains fmaf(a, a, v) over its
+ *     elements.
+ *   residual != NULL (fused_add_rms_norm): a = bf16(x + residual) (binary32
+ *     add, rounded to bf16), written back to residual; each vector's 8
+ *     squares are chained from zero, then added to the thread's partial.
+ * The device then takes r = rsqrtf(acc / n + eps), the division IEEE; rsqrtf
+ * is CUDA's and is not restated here (tests bound it instead).
+ */
+int orc_rms_sumsq(const uint16_t* x, uint16_t* residual, int64_t m, int64_t n, float* acc) {
+  if (m < 0 || n < 0 || n % 8) return -1;
+  const int threads = m < 256 ? 1024 : 256;
+  const int64_t chunks = n / 8;
+  float* part = (float*)malloc(sizeof(float) * threads);
+  if (!part) return -2;
+  for (int64_t r = 0; r < m; ++r) {
+    const uint16_t* xr = x + r * n;
+    uint16_t* rr = residual ? residual + r * n : NULL;
+    for (int t = 0; t < threads; ++t) {
+      float v = 0.0f;
+      for (int64_t c = t; c < chunks; c += threads) {
+        if (rr) {
+          float p = 0.0f;
+          for (int j = 0; j < 8; ++j) {
+            const int64_t e = c * 8 + j;
+            float z = bf16_to_f32(xr[e]) + bf16_to_f32(rr[e]);
+            uint16_t zb = encode_dtype(round_to_dtype((double)z, ORC_BF16), ORC_BF16);
+            rr[e] = zb;
+            float a = bf16_to_f32(zb);
+            p = fmaf(a, a, p);
+          }
+          v = v + p;
+        } else {
+          for (int j = 0; j < 8; ++j) {
+            float a = bf16_to_f32(xr[c * 8 + j]);
+            v = fmaf(a, a, v);
+          }
+        }
+      }
+      part[t] = v;
+    }
+    float total = 0.0f;
+    for (int w = 0; w < threads / 32; ++w) {
+      float lane[32];
+      memcpy(lane, part + w * 32, sizeof(lane));
+      for (int o = 1; o < 32; o <<= 1)
+        for (int i = 0; i + o < 32; ++i) lane[i] = lane[i] + lane[i + o]; /* reads i+o before it changes */
+      total = w == 0 ? lane[0] : total + lane[0];
+    }
+    acc[r] = total;
+  }
+  free(part);
+  return 0;
+}
+
+/* RMSNorm's output given each row's r: bf16(RN(RN(x * r) * w)). */
+int orc_rms_apply(const uint16_t* x, const uint16_t* weight, const float* rstd, int64_t m,
+                  int64_t n, uint16_t* out) {
+  if (m < 0 || n < 0) return -1;
+  for (int64_t r = 0; r < m; ++r)
+    for (int64_t c = 0; c < n; ++c) {
+      float y = (bf16_to_f32(x[r * n + c]) * rstd[r]) * bf16_to_f32(weight[c]);
+      out[r * n + c] = encode_dtype(round_to_dtype((double)y, ORC_BF16), ORC_BF16);
     }
   return 0;
 }

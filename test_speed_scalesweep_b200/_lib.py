@@ -30,6 +30,8 @@ _SIGNATURES = {
     "ssw_scalesweep128_nvfp4_quant_out": (_int, [_c_p, _int, _i64, _i64, _i64, _c_p, _c_p, _c_p, _int, _c_p]),
     "ssw_rtn_nvfp4_quant_out": (_int, [_c_p, _int, _i64, _i64, _i64, _c_p, _c_p, _c_p, _int, _c_p]),
     "ssw_silu_and_mul": (_int, [_c_p, _int, _i64, _i64, _c_p, _c_p]),
+    "ssw_rms_norm_scalesweep_mse_nvfp4_quant_out": (_int, [_c_p, _c_p, _c_p, _f32, _i64, _i64, _c_p,
+                                                           _c_p, _c_p, _int, _c_p, _c_p]),
     "ssw_silu_and_mul_scalesweep_mse_nvfp4_quant_out": (_int, [_c_p, _int, _i64, _i64, _c_p, _c_p,
                                                                _c_p, _int, _c_p]),
     "ssw_absmax_workspace_bytes": (_i64, []),

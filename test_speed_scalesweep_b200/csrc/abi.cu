@@ -54,7 +54,8 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 int quant_out(const char* name, int variant, int mode, const void* input, int input_dtype,
               int64_t num_rows, int64_t n, int64_t physical_n, const float* input_scale,
               uint8_t* output, uint8_t* output_scale, int swizzled, void* stream,
-              bool silu_mul = false) {
+              bool silu_mul = false, const uint16_t* norm_weight = nullptr,
+              const float* norm_rstd = nullptr) {
   g_last_error.clear();
   if (input_dtype != SSW_DTYPE_BF16 && input_dtype != SSW_DTYPE_F16)
     return fail(SSW_ERR_INVALID_ARGUMENT, "%s: input dtype must be bf16 or f16 (got %d)", name,
@@ -99,6 +100,8 @@ int quant_out(const char* name, int variant, int mode, const void* input, int in
   p.swizzled = swizzled ? 1 : 0;
   p.scale_word_stores = (bpc_out % 4 == 0) && aligned(output_scale, 4);
   p.silu_row_elems = silu_mul ? 2 * (uint64_t)n : 0;
+  p.norm_weight = norm_weight;
+  p.norm_rstd = norm_rstd;
   const bool vec = aligned(input, 32) && aligned(output, 8);
   if (silu_mul && !vec)
     return fail(SSW_ERR_INVALID_ARGUMENT,
@@ -110,10 +113,11 @@ int quant_out(const char* name, int variant, int mode, const void* input, int in
   const int lanes = ssw::quant_lanes_per_block(nblocks, sms, mode, vec);
   const int grid = ssw::quant_grid_size(nblocks, sms, lanes);
   cudaError_t e =
-      silu_mul ? ssw::launch_silu_mul_quant(p, input_dtype, lanes, grid,
-                                            static_cast<cudaStream_t>(stream))
-               : ssw::launch_quant(p, variant, mode, input_dtype, vec, lanes, grid,
-                                   static_cast<cudaStream_t>(stream));
+      silu_mul      ? ssw::launch_silu_mul_quant(p, input_dtype, lanes, grid,
+                                                 static_cast<cudaStream_t>(stream))
+      : norm_weight ? ssw::launch_norm_quant(p, lanes, grid, static_cast<cudaStream_t>(stream))
+                    : ssw::launch_quant(p, variant, mode, input_dtype, vec, lanes, grid,
+                                        static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, name);
   return SSW_OK;
 }
@@ -315,6 +319,49 @@ int ssw_silu_and_mul_scalesweep_mse_nvfp4_quant_out(const void* input, int input
   return quant_out("silu_and_mul_scalesweep_mse_nvfp4_quant_out", ssw::kVariantMse,
                    ssw::kModeWindow, input, input_dtype, num_rows, n, n, input_scale, output,
                    output_scale, is_sf_swizzled_layout, stream, /*silu_mul=*/true);
+}
+
+int ssw_rms_norm_scalesweep_mse_nvfp4_quant_out(const void* input, void* residual,
+                                                const void* weight, float eps, int64_t num_rows,
+                                                int64_t n, const float* input_scale,
+                                                uint8_t* output, uint8_t* output_scale,
+                                                int is_sf_swizzled_layout, float* rstd_workspace,
+                                                void* stream) {
+  g_last_error.clear();
+  const char* name = "rms_norm_scalesweep_mse_nvfp4_quant_out";
+  if (num_rows < 0 || n <= 0) return fail(SSW_ERR_INVALID_ARGUMENT, "%s: bad sizes", name);
+  if (n % 16)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: n must be a multiple of 16 (got %lld)", name,
+                (long long)n);
+  // every check the quantizer makes is made here too, before the statistics
+  // kernel runs: a call that fails leaves the residual untouched
+  if (num_rows >= (1ll << 31) || n >= (1ll << 31) ||
+      (uint64_t)num_rows * (uint64_t)(n / 16) >= (1ull << 32))
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: sizes must be below 2^31 and blocks below 2^32",
+                name);
+  if (num_rows == 0) return SSW_OK;
+  if (!input || !weight || !rstd_workspace || !input_scale || !output || !output_scale)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (!aligned(input, 32) || !aligned(weight, 32) || (residual && !aligned(residual, 32)) ||
+      !aligned(rstd_workspace, 4) || !aligned(input_scale, 4) || !aligned(output, 8))
+    return fail(SSW_ERR_INVALID_ARGUMENT,
+                "%s: input, residual and weight must be 32-byte aligned, output 8-byte, "
+                "input_scale and rstd_workspace 4-byte", name);
+  int sms = 0;
+  const int sst = device_sms(&sms);
+  if (sst != SSW_OK) return sst;
+  // vLLM launches 1024 threads per token below 256 tokens and 256 from there
+  const int vllm_threads = num_rows < 256 ? 1024 : 256;
+  cudaError_t e = ssw::launch_rms_stats(static_cast<const uint16_t*>(input),
+                                        static_cast<uint16_t*>(residual), (uint64_t)num_rows,
+                                        (uint32_t)n, eps, vllm_threads, rstd_workspace,
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, name);
+  // the normalised values come from the updated residual in the fused-add form
+  return quant_out(name, ssw::kVariantMse, ssw::kModeWindow, residual ? residual : input,
+                   SSW_DTYPE_BF16, num_rows, n, n, input_scale, output, output_scale,
+                   is_sf_swizzled_layout, stream, false, static_cast<const uint16_t*>(weight),
+                   rstd_workspace);
 }
 
 int ssw_rtn_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows, int64_t n,

@@ -176,6 +176,17 @@ __device__ __forceinline__ uint32_t silu_mul2(uint32_t g, uint32_t u) {
   }
 }
 
+// vLLM's RMSNorm output for a word of two bf16 values: bf16((x * r) * w),
+// the two products rounded in binary32 (vllm 0.22 rms_norm and
+// fused_add_rms_norm, registered for model_executor/layers/layernorm.py;
+// matched bit for bit on B200).
+__device__ __forceinline__ uint32_t rms_norm2(uint32_t x, uint32_t w, float r) {
+  const float x0 = __uint_as_float(x << 16), x1 = __uint_as_float(x & 0xFFFF0000u);
+  const float w0 = __uint_as_float(w << 16), w1 = __uint_as_float(w & 0xFFFF0000u);
+  const __nv_bfloat162 h = __floats2bfloat162_rn(mul_rn(mul_rn(x0, r), w0), mul_rn(mul_rn(x1, r), w1));
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 __device__ __forceinline__ void consider(float mse, int raw, float& best, int& best_raw) {
   // strict '<': NaN never wins and ties keep the earlier (lower-index) candidate
   if (mse < best) {
@@ -250,11 +261,13 @@ __device__ __forceinline__ void merge_best(float& best, int& bi, float ob, int o
 // the throughput configuration: one lane per block, all 11 candidates.
 // kSiluMul: the block's 16 values are h = silu(gate) * up, formed from the
 // gate and up halves of a [rows, 2n] input (silu_mul2) instead of loaded.
-template <int kVariant, int kMode, int kDType, bool kVec, int kLanes, bool kSiluMul = false>
+template <int kVariant, int kMode, int kDType, bool kVec, int kLanes, bool kSiluMul = false,
+          bool kNorm = false>
 __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantParams p) {
   static_assert(kLanes == 1 || (kMode == kModeWindow && (kLanes == 2 || kLanes == 4)),
                 "lane sharing applies to the 11-candidate window only");
   static_assert(!kSiluMul || kVec, "the SiLU-and-mul input is read with vector loads");
+  static_assert(!kNorm || (kVec && kDType == kDTypeBF16), "the RMSNorm front end is bf16, vector");
   // A GEMM launched as this grid's programmatic dependent may start its
   // prologue now; it reads the codes only after griddepcontrol.wait, which
   // waits for this whole grid to finish.
@@ -313,6 +326,14 @@ __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantP
         ld_block_v8(gate + (uint64_t)bpc_in * 16, u);
 #pragma unroll
         for (int j = 0; j < 8; ++j) w[j] = silu_mul2<kDType>(g[j], u[j]);
+      } else if constexpr (kNorm) {
+        const uint16_t* src = p.input + ((uint64_t)row * bpc_in + col) * 16;
+        uint32_t xw[8], ww[8];
+        ld_block_v8(src, xw);
+        ld_block_v8(p.norm_weight + (uint64_t)col * 16, ww);
+        const float r = __ldg(p.norm_rstd + row);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = rms_norm2(xw[j], ww[j], r);
       } else {
         const uint16_t* src = p.input + ((uint64_t)row * bpc_in + col) * 16;
         if constexpr (kVec) {
@@ -463,10 +484,83 @@ __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantP
   }
 }
 
-template <int kVariant, int kMode, int kDType, bool kVec, int kLanes, bool kSiluMul = false>
+template <int kVariant, int kMode, int kDType, bool kVec, int kLanes, bool kSiluMul = false,
+          bool kNorm = false>
 cudaError_t launch_one(const QuantParams& p, int grid, cudaStream_t stream) {
-  quant_kernel<kVariant, kMode, kDType, kVec, kLanes, kSiluMul><<<grid, kThreads, 0, stream>>>(p);
+  quant_kernel<kVariant, kMode, kDType, kVec, kLanes, kSiluMul, kNorm>
+      <<<grid, kThreads, 0, stream>>>(p);
   return cudaGetLastError();
+}
+
+// vLLM's RMSNorm statistics for one row per CTA.  vLLM launches one block of
+// kVllmThreads threads per token; its thread t takes the 8-element vectors
+// t, t + T, ... of the row, and a CUB block reduction (shuffle-down tree with
+// offsets 1..16 in each warp, then the warp sums in order) adds the threads'
+// partials.  The 256 threads here each play kVllmThreads / 256 of vLLM's
+// threads, keeping every partial and every tree exactly as vLLM forms them.
+// kAdd (fused_add_rms_norm): v = bf16(x + residual), written back to the
+// residual; each vector's 8 squares are summed from zero before joining the
+// thread's partial.  Otherwise (rms_norm) the squares chain straight into it.
+template <int kVllmThreads, bool kAdd>
+__global__ void __launch_bounds__(kThreads) rms_stats_kernel(const uint16_t* __restrict__ x,
+                                                             uint16_t* __restrict__ residual,
+                                                             uint32_t n, float eps,
+                                                             float* __restrict__ rstd) {
+  constexpr int kVirt = kVllmThreads / kThreads;  // vLLM threads per thread here
+  static_assert(kVirt >= 1 && kVllmThreads % kThreads == 0, "thread mapping");
+  __shared__ float warp_sums[kVllmThreads / 32];
+  const uint64_t base = (uint64_t)blockIdx.x * n;
+  const uint32_t chunks = n / 8, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int q = 0; q < kVirt; ++q) {
+    const uint32_t t = threadIdx.x + q * kThreads;  // vLLM's thread index
+    float v = 0.0f;
+    for (uint32_t c = t; c < chunks; c += kVllmThreads) {
+      const uint4 xa = *reinterpret_cast<const uint4*>(x + base + (uint64_t)c * 8);
+      const uint32_t xw[4] = {xa.x, xa.y, xa.z, xa.w};
+      if constexpr (kAdd) {
+        uint4* rp = reinterpret_cast<uint4*>(residual + base + (uint64_t)c * 8);
+        const uint4 ra = *rp;
+        const uint32_t rw[4] = {ra.x, ra.y, ra.z, ra.w};
+        uint32_t zw[4];
+        float part = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float z0 = add_rn(__uint_as_float(xw[k] << 16), __uint_as_float(rw[k] << 16));
+          const float z1 = add_rn(__uint_as_float(xw[k] & 0xFFFF0000u),
+                                  __uint_as_float(rw[k] & 0xFFFF0000u));
+          const __nv_bfloat162 zb = __floats2bfloat162_rn(z0, z1);
+          zw[k] = *reinterpret_cast<const uint32_t*>(&zb);
+          const float a0 = __uint_as_float(zw[k] << 16), a1 = __uint_as_float(zw[k] & 0xFFFF0000u);
+          part = fma_rn(a0, a0, part);
+          part = fma_rn(a1, a1, part);
+        }
+        *rp = make_uint4(zw[0], zw[1], zw[2], zw[3]);
+        v = add_rn(v, part);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float a0 = __uint_as_float(xw[k] << 16), a1 = __uint_as_float(xw[k] & 0xFFFF0000u);
+          v = fma_rn(a0, a0, v);
+          v = fma_rn(a1, a1, v);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float other = __shfl_down_sync(0xFFFFFFFFu, v, o);
+      if (lane + o < 32) v = add_rn(v, other);
+    }
+    if (lane == 0) warp_sums[wid + q * (kThreads / 32)] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float acc = warp_sums[0];
+    for (int k = 1; k < kVllmThreads / 32; ++k) acc = add_rn(acc, warp_sums[k]);
+    float mean;
+    asm("div.rn.f32 %0, %1, %2;" : "=f"(mean) : "f"(acc), "f"((float)n));
+    rstd[blockIdx.x] = rsqrtf(add_rn(mean, eps));
+  }
 }
 
 template <int kDType>
@@ -537,6 +631,35 @@ cudaError_t launch_silu_mul_quant(const QuantParams& p, int dtype, int lanes, in
                                   cudaStream_t stream) {
   if (dtype == kDTypeBF16) return launch_silu_lanes<kDTypeBF16>(p, lanes, grid, stream);
   return launch_silu_lanes<kDTypeF16>(p, lanes, grid, stream);
+}
+
+cudaError_t launch_norm_quant(const QuantParams& p, int lanes, int grid, cudaStream_t stream) {
+  if (lanes == 4)
+    return launch_one<kVariantMse, kModeWindow, kDTypeBF16, true, 4, false, true>(p, grid, stream);
+  if (lanes == 2)
+    return launch_one<kVariantMse, kModeWindow, kDTypeBF16, true, 2, false, true>(p, grid, stream);
+  if (lanes != 1) return cudaErrorInvalidValue;
+  return launch_one<kVariantMse, kModeWindow, kDTypeBF16, true, 1, false, true>(p, grid, stream);
+}
+
+cudaError_t launch_rms_stats(const uint16_t* x, uint16_t* residual, uint64_t rows, uint32_t n,
+                             float eps, int vllm_threads, float* rstd, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  const dim3 grid((unsigned)rows);
+  if (vllm_threads == 1024) {
+    if (residual)
+      rms_stats_kernel<1024, true><<<grid, kThreads, 0, stream>>>(x, residual, n, eps, rstd);
+    else
+      rms_stats_kernel<1024, false><<<grid, kThreads, 0, stream>>>(x, residual, n, eps, rstd);
+  } else if (vllm_threads == 256) {
+    if (residual)
+      rms_stats_kernel<256, true><<<grid, kThreads, 0, stream>>>(x, residual, n, eps, rstd);
+    else
+      rms_stats_kernel<256, false><<<grid, kThreads, 0, stream>>>(x, residual, n, eps, rstd);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
 }
 
 cudaError_t launch_silu_mul(const uint16_t* input, uint16_t* output, uint64_t rows, uint32_t n,

@@ -25,6 +25,8 @@ struct QuantParams {
   int swizzled;
   int scale_word_stores;      // bpc_out % 4 == 0 and output_scale 4-byte aligned
   uint64_t silu_row_elems;    // SiLU-and-mul input only: elements per input row (2 * n)
+  const uint16_t* norm_weight;  // RMSNorm front end only: bf16 weight [n]
+  const float* norm_rstd;       // RMSNorm front end only: 1/rms of each row [rows]
 };
 
 // Lanes sharing one block (1, 2 or 4): more than 1 only for the 11-candidate
@@ -40,6 +42,16 @@ cudaError_t launch_quant(const QuantParams& p, int variant, int mode, int dtype,
 // vLLM's silu_and_mul computes it.  Vector loads only (input 32-byte aligned).
 cudaError_t launch_silu_mul_quant(const QuantParams& p, int dtype, int lanes, int grid,
                                   cudaStream_t stream);
+// The "scalesweep_mse" window quantizer on h = bf16(x * rstd[row] * weight)
+// of a bf16 input [rows, n] (RMSNorm's output, formed on the fly).  Vector
+// loads only; rstd from launch_rms_stats.
+cudaError_t launch_norm_quant(const QuantParams& p, int lanes, int grid, cudaStream_t stream);
+// vLLM's RMSNorm statistics, per row: rstd[row] = rsqrtf(mean(v^2) + eps) in
+// the reduction order of vLLM's rms_norm (residual == nullptr, v = x) or of
+// its fused_add_rms_norm (v = bf16(x + residual), written back to residual).
+// vllm_threads is the block size vLLM would launch (1024 or 256).
+cudaError_t launch_rms_stats(const uint16_t* x, uint16_t* residual, uint64_t rows, uint32_t n,
+                             float eps, int vllm_threads, float* rstd, cudaStream_t stream);
 // The SiLU-and-mul alone: output [rows, n] = silu(input[:, :n]) * input[:, n:].
 cudaError_t launch_silu_mul(const uint16_t* input, uint16_t* output, uint64_t rows, uint32_t n,
                             int dtype, int device_sms, cudaStream_t stream);

@@ -14,6 +14,7 @@ from __future__ import annotations
 import torch
 
 from . import act_quant
+from . import norm_quant
 from . import scalesweep_mse_nvfp4_utils as mse
 from . import scalesweep_mse_reference_nvfp4_utils as mse_ref
 from . import scalesweep_nvfp4_utils as sweep
@@ -92,6 +93,7 @@ def _register(namespace: str, kind: str) -> None:
         torch.library.register_fake(f"{namespace}::{name}.out", fake_out, lib=lib)
     if namespace == NAMESPACE:
         _register_act_quant(lib, namespace)
+        _register_norm_quant(lib, namespace)
         _register_linear(lib, namespace)
     _libs[namespace] = lib
 
@@ -155,6 +157,51 @@ def _register_act_quant(lib: torch.library.Library, namespace: str) -> None:
     torch.library.register_fake(f"{namespace}::{fused}.out", fake_none, lib=lib)
     torch.library.register_fake(f"{namespace}::silu_and_mul", fake_none, lib=lib)
     torch.library.register_fake(f"{namespace}::silu_and_mul_nvfp4_quant", fake_none, lib=lib)
+
+
+def _register_norm_quant(lib: torch.library.Library, namespace: str) -> None:
+    """RMSNorm fused into the scale-sweep quantizer (norm_quant.py).  The
+    in-place forms follow vLLM's fused RMSNorm + quant schemas
+    (``rms_norm_static_fp8_quant(result, input, weight, scale, epsilon)``,
+    ``fused_add_rms_norm_static_fp8_quant(result, input, residual, weight,
+    scale, epsilon)``) with the swizzled block-scale tensor after ``result``,
+    as in ``silu_and_mul_nvfp4_quant``."""
+    fn = "rms_norm_scalesweep_mse_nvfp4_quant"
+    lib.define(fn + "(Tensor input, Tensor weight, float epsilon, Tensor input_scale, "
+               "bool is_sf_swizzled_layout=True) -> (Tensor, Tensor)")
+    lib.define("rms_norm_nvfp4_quant(Tensor(a!) result, Tensor(b!) result_block_scale, "
+               "Tensor input, Tensor weight, Tensor input_global_scale, float epsilon) -> ()")
+    lib.define("fused_add_rms_norm_nvfp4_quant(Tensor(a!) result, Tensor(b!) result_block_scale, "
+               "Tensor input, Tensor(c!) residual, Tensor weight, Tensor input_global_scale, "
+               "float epsilon) -> ()")
+
+    def functional(input, weight, epsilon, input_scale, is_sf_swizzled_layout=True):
+        return norm_quant.rms_norm_scalesweep_mse_nvfp4_quant(input, weight, epsilon, input_scale,
+                                                              is_sf_swizzled_layout)
+
+    def norm_q(result, result_block_scale, input, weight, input_global_scale, epsilon):
+        norm_quant.rms_norm_scalesweep_mse_nvfp4_quant_out(
+            input, weight, epsilon, input_global_scale, True, output=result,
+            output_scale=result_block_scale)
+
+    def add_norm_q(result, result_block_scale, input, residual, weight, input_global_scale,
+                   epsilon):
+        norm_quant.rms_norm_scalesweep_mse_nvfp4_quant_out(
+            input, weight, epsilon, input_global_scale, True, output=result,
+            output_scale=result_block_scale, residual=residual)
+
+    def fake_functional(input, weight, epsilon, input_scale, is_sf_swizzled_layout=True):
+        return norm_quant.alloc_outputs(input, is_sf_swizzled_layout)
+
+    def fake_none(*args, **kwargs):
+        return None
+
+    lib.impl(fn, functional, "CUDA")
+    lib.impl("rms_norm_nvfp4_quant", norm_q, "CUDA")
+    lib.impl("fused_add_rms_norm_nvfp4_quant", add_norm_q, "CUDA")
+    torch.library.register_fake(f"{namespace}::{fn}", fake_functional, lib=lib)
+    torch.library.register_fake(f"{namespace}::rms_norm_nvfp4_quant", fake_none, lib=lib)
+    torch.library.register_fake(f"{namespace}::fused_add_rms_norm_nvfp4_quant", fake_none, lib=lib)
 
 
 def register() -> None:
