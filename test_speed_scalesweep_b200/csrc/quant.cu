@@ -298,6 +298,12 @@ __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantP
     }
   }
   __syncthreads();
+  if constexpr (kNorm) {
+    // Launched as a programmatic dependent of rms_stats_kernel: the tables
+    // above were built while it ran; r and the updated residual are read
+    // only after it has finished and its writes are visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+  }
 
   const float gsi = __ldg(p.input_scale);
   const float abs_gsi = fabsf(gsi);
@@ -507,21 +513,39 @@ __global__ void __launch_bounds__(kThreads) rms_stats_kernel(const uint16_t* __r
                                                              uint32_t n, float eps,
                                                              float* __restrict__ rstd) {
   constexpr int kVirt = kVllmThreads / kThreads;  // vLLM threads per thread here
-  static_assert(kVirt >= 1 && kVllmThreads % kThreads == 0, "thread mapping");
+  static_assert(kVirt >= 1 && kVllmThreads % kThreads == 0 && 4 % kVirt == 0, "thread mapping");
+  constexpr int kRounds = 4 / kVirt;        // strides of kVllmThreads vectors per pass
+  constexpr int kLoads = kVirt * kRounds;   // 4 vectors of 16 bytes (per input) in flight
+  // The quantizer launched after this grid may start (its table prologue)
+  // once every CTA here has started.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ float warp_sums[kVllmThreads / 32];
   const uint64_t base = (uint64_t)blockIdx.x * n;
   const uint32_t chunks = n / 8, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float v[kVirt];
 #pragma unroll
-  for (int q = 0; q < kVirt; ++q) {
-    const uint32_t t = threadIdx.x + q * kThreads;  // vLLM's thread index
-    float v = 0.0f;
-    for (uint32_t c = t; c < chunks; c += kVllmThreads) {
-      const uint4 xa = *reinterpret_cast<const uint4*>(x + base + (uint64_t)c * 8);
-      const uint32_t xw[4] = {xa.x, xa.y, xa.z, xa.w};
+  for (int q = 0; q < kVirt; ++q) v[q] = 0.0f;
+  // Each pass issues all its loads first, then adds them in.  Virtual thread
+  // q still takes its vectors t, t + T, t + 2T, ... in that order, so every
+  // partial is formed exactly as vLLM forms it.
+  for (uint32_t first = 0; first < chunks; first += kRounds * kVllmThreads) {
+    uint4 xa[kLoads], ra[kLoads];
+#pragma unroll
+    for (int i = 0; i < kLoads; ++i) {
+      const uint32_t c = first + (i / kVirt) * kVllmThreads + threadIdx.x + (i % kVirt) * kThreads;
+      if (c < chunks) {
+        xa[i] = *reinterpret_cast<const uint4*>(x + base + (uint64_t)c * 8);
+        if constexpr (kAdd) ra[i] = *reinterpret_cast<const uint4*>(residual + base + (uint64_t)c * 8);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kLoads; ++i) {
+      const int q = i % kVirt;
+      const uint32_t c = first + (i / kVirt) * kVllmThreads + threadIdx.x + q * kThreads;
+      if (c >= chunks) continue;
+      const uint32_t xw[4] = {xa[i].x, xa[i].y, xa[i].z, xa[i].w};
       if constexpr (kAdd) {
-        uint4* rp = reinterpret_cast<uint4*>(residual + base + (uint64_t)c * 8);
-        const uint4 ra = *rp;
-        const uint32_t rw[4] = {ra.x, ra.y, ra.z, ra.w};
+        const uint32_t rw[4] = {ra[i].x, ra[i].y, ra[i].z, ra[i].w};
         uint32_t zw[4];
         float part = 0.0f;
 #pragma unroll
@@ -535,23 +559,28 @@ __global__ void __launch_bounds__(kThreads) rms_stats_kernel(const uint16_t* __r
           part = fma_rn(a0, a0, part);
           part = fma_rn(a1, a1, part);
         }
-        *rp = make_uint4(zw[0], zw[1], zw[2], zw[3]);
-        v = add_rn(v, part);
+        *reinterpret_cast<uint4*>(residual + base + (uint64_t)c * 8) =
+            make_uint4(zw[0], zw[1], zw[2], zw[3]);
+        v[q] = add_rn(v[q], part);
       } else {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const float a0 = __uint_as_float(xw[k] << 16), a1 = __uint_as_float(xw[k] & 0xFFFF0000u);
-          v = fma_rn(a0, a0, v);
-          v = fma_rn(a1, a1, v);
+          v[q] = fma_rn(a0, a0, v[q]);
+          v[q] = fma_rn(a1, a1, v[q]);
         }
       }
     }
+  }
+#pragma unroll
+  for (int q = 0; q < kVirt; ++q) {
+    float w = v[q];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const float other = __shfl_down_sync(0xFFFFFFFFu, v, o);
-      if (lane + o < 32) v = add_rn(v, other);
+      const float other = __shfl_down_sync(0xFFFFFFFFu, w, o);
+      if (lane + o < 32) w = add_rn(w, other);
     }
-    if (lane == 0) warp_sums[wid + q * (kThreads / 32)] = v;
+    if (lane == 0) warp_sums[wid + q * (kThreads / 32)] = w;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -633,13 +662,29 @@ cudaError_t launch_silu_mul_quant(const QuantParams& p, int dtype, int lanes, in
   return launch_silu_lanes<kDTypeF16>(p, lanes, grid, stream);
 }
 
+// The RMSNorm quantizer is a programmatic dependent launch of the statistics
+// kernel before it on the stream (it waits with griddepcontrol.wait).
+template <int kLanes>
+cudaError_t launch_norm_lanes(const QuantParams& p, int grid, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(
+      &cfg, quant_kernel<kVariantMse, kModeWindow, kDTypeBF16, true, kLanes, false, true>, p);
+}
+
 cudaError_t launch_norm_quant(const QuantParams& p, int lanes, int grid, cudaStream_t stream) {
-  if (lanes == 4)
-    return launch_one<kVariantMse, kModeWindow, kDTypeBF16, true, 4, false, true>(p, grid, stream);
-  if (lanes == 2)
-    return launch_one<kVariantMse, kModeWindow, kDTypeBF16, true, 2, false, true>(p, grid, stream);
+  if (lanes == 4) return launch_norm_lanes<4>(p, grid, stream);
+  if (lanes == 2) return launch_norm_lanes<2>(p, grid, stream);
   if (lanes != 1) return cudaErrorInvalidValue;
-  return launch_one<kVariantMse, kModeWindow, kDTypeBF16, true, 1, false, true>(p, grid, stream);
+  return launch_norm_lanes<1>(p, grid, stream);
 }
 
 cudaError_t launch_rms_stats(const uint16_t* x, uint16_t* residual, uint64_t rows, uint32_t n,

@@ -44,7 +44,8 @@ cudaError_t launch_silu_mul_quant(const QuantParams& p, int dtype, int lanes, in
                                   cudaStream_t stream);
 // The "scalesweep_mse" window quantizer on h = bf16(x * rstd[row] * weight)
 // of a bf16 input [rows, n] (RMSNorm's output, formed on the fly).  Vector
-// loads only; rstd from launch_rms_stats.
+// loads only; rstd from launch_rms_stats, which must be the launch just
+// before on the same stream: this grid is its programmatic dependent.
 cudaError_t launch_norm_quant(const QuantParams& p, int lanes, int grid, cudaStream_t stream);
 // vLLM's RMSNorm statistics, per row: rstd[row] = rsqrtf(mean(v^2) + eps) in
 // the reduction order of vLLM's rms_norm (residual == nullptr, v = x) or of
