@@ -84,8 +84,12 @@ NVFP4_QUANT_CONFIG = {
 # "scalesweep_mse_fused_act": additionally, each MLP's SiLU-and-mul and the
 # down projection's activation quantizer run as one fused kernel
 # (install_fused_act_hook), with vLLM's GEMM.
+# "scalesweep_mse_fused_norm_act": also each decoder layer's two RMSNorms are
+# fused into the qkv and gate_up projections' quantizers
+# (install_fused_norm_hook).
 BACKENDS = ("scalesweep_mse", "scalesweep_mse_reference", "rtn", "cutlass",
-            "scalesweep_mse_linear", "scalesweep_mse_fused_act")
+            "scalesweep_mse_linear", "scalesweep_mse_fused_act",
+            "scalesweep_mse_fused_norm_act")
 _OP_FOR_BACKEND = {"scalesweep_mse": "scalesweep_mse_nvfp4_quant",
                    "scalesweep_mse_reference": "scalesweep_mse_reference_nvfp4_quant",
                    "rtn": "rtn_nvfp4_quant"}
@@ -207,7 +211,6 @@ def install_fused_act_hook() -> None:
     forward.
     """
     from . import ops  # noqa: F401  (registers torch.ops.scalesweep_b200.*)
-    import vllm._custom_ops as vllm_ops
     from vllm.model_executor.models.llama import LlamaMLP
 
     original = LlamaMLP.forward
@@ -215,26 +218,121 @@ def install_fused_act_hook() -> None:
         return
 
     def forward(self, x):
-        down = self.down_proj
-        if (getattr(down, "tp_size", 1) != 1 or getattr(down, "weights_padding_cols", 0)
-                or not all(hasattr(down, a) for a in ("input_global_scale_inv",
-                                                        "weight_scale", "alpha"))
-                or down.weight.dtype != torch.uint8):
+        if not _single_gpu_w4a4(self.down_proj):
             MLP_CALLS["fallback"] += 1
             return original(self, x)
         MLP_CALLS["fused"] += 1
         gate_up, _ = self.gate_up_proj(x)
-        codes, scales = torch.ops.scalesweep_b200.silu_and_mul_scalesweep_mse_nvfp4_quant(
-            gate_up.reshape(-1, gate_up.shape[-1]), down.input_global_scale_inv, True)
-        out = vllm_ops.cutlass_scaled_fp4_mm(codes, down.weight, scales, down.weight_scale,
-                                             down.alpha, gate_up.dtype)
-        out = out[:, :down.output_size_per_partition]
-        if down.bias is not None:
-            out = out + down.bias
-        return out.view(*gate_up.shape[:-1], down.output_size_per_partition)
+        return _silu_mul_down(self.down_proj, gate_up)
 
     forward._scalesweep_b200 = True
     LlamaMLP.forward = forward
+
+
+def _single_gpu_w4a4(lin) -> bool:
+    """A vLLM NVFP4 W4A4 linear layer without tensor parallelism or weight
+    padding: the layers whose quantize + GEMM the hooks can issue themselves."""
+    return (getattr(lin, "tp_size", 1) == 1 and not getattr(lin, "weights_padding_cols", 0)
+            and all(hasattr(lin, a) for a in ("input_global_scale_inv", "weight_scale", "alpha"))
+            and lin.weight.dtype == torch.uint8)
+
+
+def _fp4_linear(lin, codes, scales, lead_shape, dtype):
+    """vLLM's CUTLASS NVFP4 GEMM on already-quantized activations, as
+    ``CutlassNvFp4LinearKernel.apply_weights`` runs it after quantizing
+    (vllm 0.22 ``model_executor/kernels/linear/nvfp4/cutlass.py:64-77``)."""
+    import vllm._custom_ops as vllm_ops
+    out = vllm_ops.cutlass_scaled_fp4_mm(codes, lin.weight, scales, lin.weight_scale, lin.alpha,
+                                         dtype)
+    out = out[:, :lin.output_size_per_partition]
+    if lin.bias is not None:
+        out = out + lin.bias
+    return out.view(*lead_shape, lin.output_size_per_partition)
+
+
+def _silu_mul_down(down, gate_up):
+    """down_proj(silu_and_mul(gate_up)) with the SiLU-and-mul fused into the
+    down projection's scale-sweep quantizer."""
+    codes, scales = torch.ops.scalesweep_b200.silu_and_mul_scalesweep_mse_nvfp4_quant(
+        gate_up.reshape(-1, gate_up.shape[-1]), down.input_global_scale_inv, True)
+    return _fp4_linear(down, codes, scales, gate_up.shape[:-1], gate_up.dtype)
+
+
+DECODER_CALLS = {"fused": 0, "fallback": 0}
+
+
+def install_fused_norm_hook() -> None:
+    """Fuse each Llama decoder layer's RMSNorms into the next projection's
+    activation quantizer, and its SiLU-and-mul into the down projection's.
+
+    ``LlamaDecoderLayer.forward`` (vllm 0.22 ``model_executor/models/llama.py:316-333``)
+    runs input_layernorm, attention (qkv_proj, rotary, attention, o_proj:
+    ``:223-233``), post_attention_layernorm and the MLP.  The replacement
+    hands each norm's input (and the residual) to ``rms_norm_nvfp4_quant`` /
+    ``fused_add_rms_norm_nvfp4_quant`` with the qkv or gate_up projection's
+    activation global scale, then runs vLLM's GEMM on the codes: the role
+    vLLM's ``fuse_norm_quant`` pass plays for its FP8 quantizers.  The
+    residual is updated in place, as ``fused_add_rms_norm`` updates it.
+
+    The normalised values are those of vLLM's ``vllm_c`` RMSNorm kernels.
+    Under Inductor vLLM runs its native RMSNorm, compiled by Inductor, whose
+    reduction order may differ in the last bits.  Layers whose projections
+    are not single-GPU NVFP4 W4A4 linears keep the original forward.
+    """
+    from . import ops  # noqa: F401  (registers torch.ops.scalesweep_b200.*)
+    from vllm.model_executor.models.llama import LlamaDecoderLayer
+
+    original = LlamaDecoderLayer.forward
+    if getattr(original, "_scalesweep_b200", False):
+        return
+
+    def norm_quant(norm, lin, x2, residual2):
+        m, n = x2.shape
+        codes = x2.new_empty((m, n // 2), dtype=torch.uint8)
+        scales = x2.new_empty(((m + 127) // 128 * 128, (n // 16 + 3) // 4 * 4),
+                              dtype=torch.float8_e4m3fn)
+        if residual2 is None:
+            torch.ops.scalesweep_b200.rms_norm_nvfp4_quant(
+                codes, scales, x2, norm.weight, lin.input_global_scale_inv,
+                norm.variance_epsilon)
+        else:
+            torch.ops.scalesweep_b200.fused_add_rms_norm_nvfp4_quant(
+                codes, scales, x2, residual2, norm.weight, lin.input_global_scale_inv,
+                norm.variance_epsilon)
+        return codes, scales
+
+    def plain_norm(norm) -> bool:
+        return (getattr(norm, "variance_size_override", None) is None
+                and getattr(norm, "has_weight", True) and norm.weight.dtype == torch.bfloat16)
+
+    def forward(self, positions, hidden_states, residual):
+        attn, mlp = self.self_attn, self.mlp
+        if not (hidden_states.dtype == torch.bfloat16 and _single_gpu_w4a4(attn.qkv_proj)
+                and _single_gpu_w4a4(mlp.gate_up_proj) and _single_gpu_w4a4(mlp.down_proj)
+                and plain_norm(self.input_layernorm)
+                and plain_norm(self.post_attention_layernorm)):
+            DECODER_CALLS["fallback"] += 1
+            return original(self, positions, hidden_states, residual)
+        DECODER_CALLS["fused"] += 1
+        lead, hidden = hidden_states.shape[:-1], hidden_states.shape[-1]
+        x2 = hidden_states.reshape(-1, hidden)
+        if residual is None:
+            residual = hidden_states
+            codes, scales = norm_quant(self.input_layernorm, attn.qkv_proj, x2, None)
+        else:
+            codes, scales = norm_quant(self.input_layernorm, attn.qkv_proj, x2,
+                                       residual.view(-1, hidden))
+        qkv = _fp4_linear(attn.qkv_proj, codes, scales, lead, hidden_states.dtype)
+        q, k, v = qkv.split([attn.q_size, attn.kv_size, attn.kv_size], dim=-1)
+        q, k = attn.rotary_emb(positions, q, k)
+        attn_out, _ = attn.o_proj(attn.attn(q, k, v))
+        codes, scales = norm_quant(self.post_attention_layernorm, mlp.gate_up_proj,
+                                   attn_out.reshape(-1, hidden), residual.view(-1, hidden))
+        gate_up = _fp4_linear(mlp.gate_up_proj, codes, scales, lead, hidden_states.dtype)
+        return _silu_mul_down(mlp.down_proj, gate_up), residual
+
+    forward._scalesweep_b200 = True
+    LlamaDecoderLayer.forward = forward
 
 
 def init_random_nvfp4_weights(model: torch.nn.Module, act_amax: float = 16.0,
@@ -276,12 +374,15 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
         gpu_memory_utilization: float = 0.85, enforce_eager: bool = False) -> dict:
     os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
     linear_ours = backend == "scalesweep_mse_linear"
-    fused_act = backend == "scalesweep_mse_fused_act"
+    fused_norm = backend == "scalesweep_mse_fused_norm_act"
+    fused_act = backend == "scalesweep_mse_fused_act" or fused_norm
     rebound = install_act_quant_hook("scalesweep_mse" if (linear_ours or fused_act) else backend)
     if linear_ours:
         install_linear_hook()
     if fused_act:
         install_fused_act_hook()
+    if fused_norm:
+        install_fused_norm_hook()
     from vllm import LLM, SamplingParams
     from vllm.inputs import TokensPrompt
 
@@ -333,6 +434,10 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
     if fused_act:
         results["mlp_hook_calls"] = dict(MLP_CALLS)
         results["fusion"] = "SiLU-and-mul + scale-sweep quant fused (this package)"
+    if fused_norm:
+        results["decoder_hook_calls"] = dict(DECODER_CALLS)
+        results["fusion"] = ("RMSNorm + scale-sweep quant (qkv, gate_up) and SiLU-and-mul + "
+                             "scale-sweep quant (down) fused (this package)")
     return results
 
 

@@ -66,3 +66,52 @@ def test_fused_act_hook_feeds_gate_up_to_the_fused_quantizer(monkeypatch):
     down.tp_size = 2                                             # tensor parallel: vLLM's path
     assert vllm_llama.LlamaMLP.forward(mlp, gate_up) == "vllm"
     assert vllm_e2e.MLP_CALLS == {"fused": 1, "fallback": 1}
+
+
+def test_fused_norm_hook_feeds_each_norm_to_the_next_projections_quantizer(monkeypatch):
+    """Layer 0 (no residual yet) takes rms_norm_nvfp4_quant, later layers
+    fused_add_rms_norm_nvfp4_quant; each GEMM sees codes of its own input
+    width, and the residual comes back."""
+    def original(self, positions, hidden_states, residual):
+        return "vllm"
+
+    monkeypatch.setattr(vllm_llama.LlamaDecoderLayer, "forward", original)
+    monkeypatch.setattr(vllm_e2e, "DECODER_CALLS", {"fused": 0, "fallback": 0})
+    mms = []
+
+    def fake_mm(a, b, sa, sb, alpha, dtype):
+        mms.append((tuple(a.shape), tuple(sa.shape), b.shape[0]))
+        return torch.empty(a.shape[0], b.shape[0], dtype=dtype, device="meta")
+
+    import vllm._custom_ops as vllm_ops
+    monkeypatch.setattr(vllm_ops, "cutlass_scaled_fp4_mm", fake_mm)
+    vllm_e2e.install_fused_norm_hook()
+    meta = dict(device="meta")
+    t, h, inter, q, kv = 5, 4096, 14336, 4096, 1024
+
+    def norm():
+        return types.SimpleNamespace(weight=torch.empty(h, dtype=torch.bfloat16, **meta),
+                                     variance_epsilon=1e-5, variance_size_override=None,
+                                     has_weight=True)
+
+    o_out = torch.empty(t, h, dtype=torch.bfloat16, **meta)
+    attn = types.SimpleNamespace(qkv_proj=_layer(n=q + 2 * kv, k=h), q_size=q, kv_size=kv,
+                                 rotary_emb=lambda pos, a, b: (a, b),
+                                 attn=lambda a, b, c: a, o_proj=lambda x: (o_out, None))
+    mlp = types.SimpleNamespace(gate_up_proj=_layer(n=2 * inter, k=h), down_proj=_layer(n=h, k=inter))
+    layer = types.SimpleNamespace(self_attn=attn, mlp=mlp, input_layernorm=norm(),
+                                  post_attention_layernorm=norm())
+    x = torch.empty(t, h, dtype=torch.bfloat16, **meta)
+    pos = torch.empty(t, dtype=torch.int64, **meta)
+    fwd = vllm_llama.LlamaDecoderLayer.forward
+    out, res = fwd(layer, pos, x, None)                    # first layer: residual = input
+    assert res is x and out.shape == (t, h)
+    res2 = torch.empty(t, h, dtype=torch.bfloat16, **meta)
+    out, res = fwd(layer, pos, x, res2)
+    assert res is res2 and out.shape == (t, h)
+    widths = [(a[1], sa, n) for a, sa, n in mms]
+    assert widths == [(h // 2, (128, h // 16), q + 2 * kv), (h // 2, (128, h // 16), 2 * inter),
+                      (inter // 2, (128, inter // 16), h)] * 2
+    mlp.down_proj.tp_size = 2                                # tensor parallel: vLLM's path
+    assert fwd(layer, pos, x, res2) == "vllm"
+    assert vllm_e2e.DECODER_CALLS == {"fused": 2, "fallback": 1}
