@@ -81,8 +81,13 @@ def test_matches_oracle(mods, m, n, add, swizzled):
     assert np.array_equal(scales.cpu().numpy(), os_)
 
 
-@pytest.mark.parametrize("m", [1, 100, 255, 256, 1000])
-@pytest.mark.parametrize("n", [4096, 14336])
+VLLM_CASES = ([(m, n) for m in (1, 100, 255, 256, 1000) for n in (4096, 14336)]
+              # widths below vLLM's block size (it launches min(n, 1024 or 256)
+              # threads) and the 70B hidden size
+              + [(3, 128), (300, 128), (5, 512), (260, 512), (3, 8192), (300, 8192)])
+
+
+@pytest.mark.parametrize("m,n", VLLM_CASES)
 @pytest.mark.parametrize("add", [False, True])
 def test_matches_vllm_then_quantize(mods, m, n, add):
     """The fused op against vLLM's RMSNorm followed by the unfused
