@@ -180,10 +180,13 @@ __device__ __forceinline__ uint32_t silu_mul2(uint32_t g, uint32_t u) {
 // the two products rounded in binary32 (vllm 0.22 rms_norm and
 // fused_add_rms_norm, registered for model_executor/layers/layernorm.py;
 // matched bit for bit on B200).
-__device__ __forceinline__ uint32_t rms_norm2(uint32_t x, uint32_t w, float r) {
-  const float x0 = __uint_as_float(x << 16), x1 = __uint_as_float(x & 0xFFFF0000u);
-  const float w0 = __uint_as_float(w << 16), w1 = __uint_as_float(w & 0xFFFF0000u);
-  const __nv_bfloat162 h = __floats2bfloat162_rn(mul_rn(mul_rn(x0, r), w0), mul_rn(mul_rn(x1, r), w1));
+// The products run as packed mul.rn.f32x2: each lane rounds as mul.rn.f32.
+__device__ __forceinline__ uint32_t rms_norm2(uint32_t x, uint32_t w, uint64_t r2) {
+  const uint64_t xp = pack2(__uint_as_float(x << 16), __uint_as_float(x & 0xFFFF0000u));
+  const uint64_t wp = pack2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+  float y0, y1;
+  unpack2(mul2(mul2(xp, r2), wp), y0, y1);
+  const __nv_bfloat162 h = __floats2bfloat162_rn(y0, y1);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
@@ -338,8 +341,9 @@ __global__ void __launch_bounds__(kThreads, kMinBlocksPerSm) quant_kernel(QuantP
         ld_block_v8(src, xw);
         ld_block_v8(p.norm_weight + (uint64_t)col * 16, ww);
         const float r = __ldg(p.norm_rstd + row);
+        const uint64_t r2 = pack2(r, r);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) w[j] = rms_norm2(xw[j], ww[j], r);
+        for (int j = 0; j < 8; ++j) w[j] = rms_norm2(xw[j], ww[j], r2);
       } else {
         const uint16_t* src = p.input + ((uint64_t)row * bpc_in + col) * 16;
         if constexpr (kVec) {
