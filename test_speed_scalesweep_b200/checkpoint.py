@@ -21,9 +21,11 @@ from a bf16 safetensors checkpoint, quantizing on the GPU:
 
 Weights are quantized with this package's RTN kernel (the rounding of
 vLLM's ``scaled_fp4_quant``), or with the scale-sweep MSE kernel.  The
-activation global scales come from a given activation amax (one value, or
-one per layer); llmcompressor's dataset calibration is not part of this
-module.
+activation global scales come from an activation amax: one value, one per
+layer, or measured by ``calibrate`` (the role of llmcompressor's
+calibration pass in ``oneshot``), which runs the bf16 model over
+calibration token ids and keeps the running max |input| of every target
+Linear on the device.
 """
 from __future__ import annotations
 
@@ -110,6 +112,43 @@ def _load_tensors(source: str) -> dict[str, torch.Tensor]:
     return out
 
 
+def calibrate(source: str, token_batches, *, targets: str = DEFAULT_TARGETS,
+              device: str = "cuda") -> dict[str, float]:
+    """Activation amax of every target Linear of the bf16 model in
+    ``source``, over forward passes on ``token_batches`` (lists of token-id
+    lists).  Returns {layer prefix: amax}, the ``act_amax`` mapping of
+    ``quantize_checkpoint``.  The model runs under transformers in bf16; a
+    forward pre-hook on each target Linear folds max |input| (this package's
+    absmax kernel) into a running maximum on the device."""
+    from transformers import AutoModelForCausalLM
+    from . import global_scale
+    if not torch.device(device).type == "cuda" or not torch.cuda.is_available():
+        raise ValueError("calibration needs a CUDA device (there is no CPU implementation)")
+    model = AutoModelForCausalLM.from_pretrained(source, dtype=torch.bfloat16).to(device)
+    model.eval()
+    pat = re.compile(targets)
+    running: dict[str, torch.Tensor] = {}
+    handles = []
+    for name, mod in model.named_modules():
+        if isinstance(mod, torch.nn.Linear) and pat.match(name + ".weight"):
+            running[name] = torch.zeros(1, dtype=torch.float32, device=device)
+
+            def hook(module, args, name=name):
+                x = args[0].contiguous()
+                torch.maximum(running[name], global_scale.absmax(x), out=running[name])
+            handles.append(mod.register_forward_pre_hook(hook))
+    try:
+        with torch.no_grad():
+            for batch in token_batches:
+                ids = torch.tensor(batch, dtype=torch.long, device=device)
+                model(input_ids=ids)
+    finally:
+        for h in handles:
+            h.remove()
+    torch.cuda.synchronize()
+    return {name: float(v.item()) for name, v in running.items()}
+
+
 def quantize_checkpoint(source: str, destination: str, *, act_amax: float | dict = 16.0,
                         weight_quantizer: str = "rtn", targets: str = DEFAULT_TARGETS,
                         device: str = "cuda") -> dict:
@@ -168,8 +207,14 @@ def main() -> None:
     ap.add_argument("--act-amax", default="16.0",
                     help="activation amax of every layer, or a JSON file {layer prefix: amax}")
     ap.add_argument("--weight-quantizer", choices=["rtn", "scalesweep_mse"], default="rtn")
+    ap.add_argument("--calibration-tokens", default=None,
+                    help="JSON file of token-id batches ([[ids, ...], ...] per batch); the "
+                         "activation amax is then measured (overrides --act-amax)")
     args = ap.parse_args()
-    if os.path.isfile(args.act_amax):
+    if args.calibration_tokens:
+        with open(args.calibration_tokens) as f:
+            act = calibrate(args.source, json.load(f))
+    elif os.path.isfile(args.act_amax):
         with open(args.act_amax) as f:
             act = {k: float(v) for k, v in json.load(f).items()}
     else:

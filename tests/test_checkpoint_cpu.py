@@ -122,3 +122,10 @@ def test_writer_refuses_without_a_gpu_and_checks_directories(tmp_path):
     if not torch.cuda.is_available():
         with pytest.raises(ValueError, match="CUDA"):
             checkpoint.quantize_checkpoint(str(tmp_path / "src"), str(tmp_path / "d2"))
+
+
+def test_calibration_refuses_without_a_gpu(tmp_path):
+    if torch.cuda.is_available():
+        pytest.skip("checks the no-GPU refusal")
+    with pytest.raises(ValueError, match="CUDA"):
+        checkpoint.calibrate(str(tmp_path), [[[1, 2, 3]]])

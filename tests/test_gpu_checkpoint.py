@@ -125,3 +125,38 @@ def test_vllm_loads_the_checkpoint(converted, tmp_path):
     assert info["gsi_in"] == gsi_in
     assert np.isclose(info["alpha"], (1.0 / gsi_in) * (1.0 / gsi_w), rtol=1e-6)
     assert len(info["tokens"]) == 4
+
+
+def test_calibration_measures_each_linears_input_amax(converted, tmp_path):
+    """calibrate() against torch hooks on the same model and tokens: the
+    amax of every target Linear's input, bit for bit (max is exact)."""
+    from transformers import AutoModelForCausalLM
+    from test_speed_scalesweep_b200 import checkpoint
+    src_dir = os.path.join(os.path.dirname(converted[1]), "src")
+    g = torch.Generator().manual_seed(7)
+    batches = [torch.randint(0, TINY["vocab_size"], (2, 24), generator=g).tolist()
+               for _ in range(3)]
+    amax = checkpoint.calibrate(src_dir, batches)
+    assert len(amax) == 14
+    model = AutoModelForCausalLM.from_pretrained(src_dir, dtype=torch.bfloat16).cuda().eval()
+    seen = {}
+    hooks = [m.register_forward_pre_hook(
+        lambda mod, args, n=n: seen.__setitem__(n, max(seen.get(n, 0.0),
+                                                       args[0].abs().max().float().item())))
+        for n, m in model.named_modules() if n in amax]
+    with torch.no_grad():
+        for b in batches:
+            model(input_ids=torch.tensor(b, device="cuda"))
+    for h in hooks:
+        h.remove()
+    assert seen.keys() == amax.keys()
+    for n in amax:
+        assert amax[n] == seen[n], n
+    p = "model.layers.0.self_attn."
+    assert amax[p + "q_proj"] == amax[p + "k_proj"] == amax[p + "v_proj"]  # one input
+    dst = str(tmp_path / "calibrated")
+    checkpoint.quantize_checkpoint(src_dir, dst, act_amax=amax)
+    from safetensors import safe_open
+    with safe_open(os.path.join(dst, "model.safetensors"), framework="pt") as h:
+        got = h.get_tensor(p + "o_proj.input_global_scale").item()
+    assert got == np.float32(oracle.global_scale_inv(amax[p + "o_proj"], 448.0))
