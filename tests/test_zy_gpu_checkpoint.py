@@ -1,7 +1,9 @@
 """GPU test of the NVFP4 checkpoint writer: a tiny Llama is written to
 safetensors, converted on the device, compared with the oracle's RTN codes
 and scales, and loaded by vLLM (in a subprocess) to check that vLLM reads
-the codes and global scales as written and generates from them."""
+the codes and global scales as written and generates from them.  It starts
+a vLLM engine and a transformers model, so it is named to run after the
+kernel parity files."""
 import json
 import os
 import subprocess
