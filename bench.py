@@ -60,6 +60,11 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
+    ap.add_argument("--no-ref-triton", action="store_true",
+                    help="skip the same-GPU timing of the reference's Triton kernels")
+    ap.add_argument("--write-config5-digests", default=None, metavar="FILE",
+                    help="one GPU: write the per-chunk SHA-256 digests of the whole tensor's "
+                         "codes and scales (the record N-GPU runs are checked against)")
     ap.add_argument("--profile-case", default=None, metavar="MxK",
                     help="only run the scale-sweep quantizer 4 times on one [M, K] input "
                          "(the command used for ncu captures) and exit")
@@ -177,6 +182,49 @@ def make_shard(rows: int, k: int, seed: int, device):
     cols = torch.randperm(k, generator=gc)[: -(-5 * k // 1000)].to(device)
     x[:, cols] *= 20
     return x
+
+
+CHUNK_ROWS = 16384  # config-5 rows are generated (and digested) in chunks of this many
+CONFIG5_SEED = 5000
+DIGEST_PATH = os.path.join(ROOT, "tests", "golden", "config5_digests.json")
+
+
+def config5_outlier_cols(k: int):
+    """The one set of ceil(0.5% * K) outlier columns of the whole config-5 tensor."""
+    import torch
+    gc = torch.Generator().manual_seed(CONFIG5_SEED ^ 0x5EED)
+    return torch.randperm(k, generator=gc)[: -(-5 * k // 1000)]
+
+
+def make_global_rows(start: int, rows: int, k: int, device):
+    """Rows [start, start + rows) of the config-5 tensor, the same bits at
+    every GPU count: chunk c (rows c*16384 ...) is N(0,1) from a generator
+    seeded with CONFIG5_SEED + c on the device, then the tensor-wide outlier
+    columns are multiplied by 20.  ``start`` and ``rows`` are whole chunks."""
+    import torch
+    if start % CHUNK_ROWS or rows % CHUNK_ROWS:
+        raise ValueError("config-5 shards are whole 16384-row chunks")
+    x = torch.empty(rows, k, dtype=torch.bfloat16, device=device)
+    for r in range(0, rows, CHUNK_ROWS):
+        g = torch.Generator(device=device).manual_seed(CONFIG5_SEED + (start + r) // CHUNK_ROWS)
+        x[r:r + CHUNK_ROWS] = torch.randn(CHUNK_ROWS, k, generator=g, device=device,
+                                          dtype=torch.float32)
+    x[:, config5_outlier_cols(k).to(device)] *= 20
+    return x
+
+
+def chunk_digests(codes, scales, start: int):
+    """SHA-256 of each 16384-row chunk's codes plus its rows of the swizzled
+    scale buffer (a contiguous slab of 128 row tiles), keyed by global chunk."""
+    import hashlib
+    out = {}
+    c_host = codes.cpu()
+    s_host = scales.view(-1, scales.shape[-1]).cpu()
+    for r in range(0, codes.shape[0], CHUNK_ROWS):
+        h = hashlib.sha256(c_host[r:r + CHUNK_ROWS].numpy().tobytes())
+        h.update(s_host[r:r + CHUNK_ROWS].numpy().tobytes())
+        out[str((start + r) // CHUNK_ROWS)] = h.hexdigest()
+    return out
 
 
 def time_events(fn, iters: int, stream):
@@ -302,6 +350,79 @@ def run_sweep(device, reps: int = 20):
             del x
     out["method"] = ("per-launch time from one CUDA graph of 20 launches, no L2 flush "
                      "(inputs of M>=16384 exceed L2)")
+    return out
+
+
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def load_reference_dispatcher():
+    """The reference's own ``bench_kernel/custom.py:nvfp4_quant`` from the
+    unmodified install under baseline/_ref (baseline/install_ref.py), with the
+    scale-sweep kernels autotuned as in its published latency runs
+    (SCALESWEEP_TUNE=1, read when the module is imported).  None if absent."""
+    if not os.path.isdir(os.path.join(REF_DIR, "bench_kernel")):
+        return None
+    os.environ.setdefault("SCALESWEEP_TUNE", "1")
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    from bench_kernel import custom as ref_custom
+    return ref_custom.nvfp4_quant
+
+
+def run_reference_triton_sweep(device, rep: int = 20):
+    """Config 2 on this GPU: the reference's Triton kernels (K1 scalesweep_mse,
+    K2 scalesweep_mse_reference) against this package's kernels, both through
+    their ``nvfp4_quant(x, gsi, True, backend)`` dispatcher and both timed with
+    the reference's method (``triton.testing.do_bench_cudagraph``, mean,
+    bench_kernel/test_kernel_latency.py:144-158).  Each shape also compares the
+    two outputs byte for byte (codes and the written scale bytes)."""
+    import torch
+    from triton.testing import do_bench_cudagraph
+    from test_speed_scalesweep_b200 import custom
+    ref_quant = load_reference_dispatcher()
+    if ref_quant is None:
+        return {"unavailable": "reference not installed under baseline/_ref"}
+    out = {"method": "triton.testing.do_bench_cudagraph(rep=20, return_mode='mean') on both "
+                     "arms' nvfp4_quant dispatchers; reference kernels autotuned "
+                     "(SCALESWEEP_TUNE=1); gsi = 256*6/amax (the reference's convention for "
+                     "scale-sweep backends)"}
+    ratios = {"scalesweep_mse": [], "scalesweep_mse_reference": []}
+    for k in SWEEP_K:
+        for m in SWEEP_M:
+            x = make_shard(m, k, 7 + m + k, device)
+            gsi = ((256.0 * 6.0) / x.abs().max().to(torch.float32)).reshape(1)
+            row = {}
+            for backend in ("scalesweep_mse", "scalesweep_mse_reference"):
+                rc, rs = ref_quant(x, gsi, True, backend)
+                oc, os_ = custom.nvfp4_quant(x, gsi, True, backend)
+                # the swizzled slab's padding rows/columns are never written by either
+                kb = k // 16
+                r_idx = torch.arange(m, device=device)[:, None]
+                c_idx = torch.arange(kb, device=device)[None, :]
+                kpad = (kb + 3) // 4 * 4
+                off = ((r_idx >> 7) * (kpad * 128) + (c_idx >> 2) * 512 + (r_idx & 31) * 16 +
+                       ((r_idx & 127) >> 5) * 4 + (c_idx & 3)).reshape(-1)
+                same = bool(torch.equal(rc, oc)) and bool(torch.equal(
+                    rs.view(torch.uint8).reshape(-1)[off], os_.view(torch.uint8).reshape(-1)[off]))
+                ref_ms = do_bench_cudagraph(lambda: ref_quant(x, gsi, True, backend), rep=rep)
+                our_ms = do_bench_cudagraph(lambda: custom.nvfp4_quant(x, gsi, True, backend),
+                                            rep=rep)
+                row[backend] = {"reference_triton_us": round(ref_ms * 1e3, 3),
+                                "ours_us": round(our_ms * 1e3, 3),
+                                "ours_over_reference_time": round(our_ms / ref_ms, 4),
+                                "bytes_equal": same}
+                ratios[backend].append(our_ms / ref_ms)
+            out[f"{m}x{k}"] = row
+            del x
+    for backend, r in ratios.items():
+        big = [v for (mk, v) in zip([f"{m}x{k}" for k in SWEEP_K for m in SWEEP_M], r)
+               if int(mk.split("x")[0]) >= 1024]
+        out[f"{backend}_geomean_time_ratio"] = round(statistics.geometric_mean(r), 4)
+        out[f"{backend}_worst_time_ratio_m_ge_1024"] = round(max(big), 4) if big else None
+    out["all_bytes_equal"] = all(v[b]["bytes_equal"] for kk, v in out.items()
+                                 if isinstance(v, dict) and "scalesweep_mse" in v
+                                 for b in ("scalesweep_mse", "scalesweep_mse_reference"))
     return out
 
 
@@ -551,7 +672,7 @@ def run_reference(args):
 def run_ours(args):
     import torch
     import torch.distributed as dist
-    from test_speed_scalesweep_b200 import _lib, custom, global_scale
+    from test_speed_scalesweep_b200 import _lib, custom, global_scale, sharded
     from test_speed_scalesweep_b200 import scalesweep_mse_nvfp4_utils as mse
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -564,12 +685,16 @@ def run_ours(args):
     _lib.lib()  # fail loudly if the CUDA library is missing
     if world > 1:
         from datetime import timedelta
+        # NCCL's init lines (rank count, NVLink/NVLS transport) go to stderr
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
-    if args.rows % (128 * world):
-        raise SystemExit("rows must be a multiple of 128 * world_size")
+    if args.rows % (CHUNK_ROWS * world):
+        raise SystemExit(f"rows must be a multiple of {CHUNK_ROWS} * world_size")
     rows = args.rows // world
     k = K_DIM
-    x = make_shard(rows, k, 1000 + rank, device)
+    row0 = rank * rows
+    x = make_global_rows(row0, rows, k, device)
     codes, scales = custom.create_fp4_output_tensors(rows, k, device, True)
     amax = torch.empty(1, dtype=torch.float32, device=device)
     gsi = torch.empty(1, dtype=torch.float32, device=device)
@@ -580,7 +705,7 @@ def run_ours(args):
             global_scale.global_scale_inv_from_max(inp, FP8_MAX, out=gsi)
         else:
             global_scale.absmax(inp, out=amax)
-            dist.all_reduce(amax, op=dist.ReduceOp.MAX)
+            sharded.all_reduce_amax(amax)
             global_scale.global_scale_from_amax(amax, FP8_MAX, out=gsi)
         mse.scalesweep_mse_nvfp4_quant_out(inp, gsi, True, output=codes, output_scale=scales)
 
@@ -646,18 +771,26 @@ def run_ours(args):
     clk = (clocks or {}).get("sm_mhz") or sm_max
     alu_peak_gbs = (SM_COUNT * FP32_LANES_PER_SM * clk * 1e6 / ALU_OPS_PER_ELEM) * \
         BYTES_PER_ELEM / 1e9
-    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})",
+    # The binding roofline is the slower of HBM and the sweep's FP32-ALU bound
+    # (35 FP32 operations per element at 148 SMs x 128 lanes x the SM clock
+    # sampled during the timed region), both in algorithmic GB/s.
+    bound = "alu" if alu_peak_gbs < hbm_peak else "hbm"
+    peak = min(alu_peak_gbs, hbm_peak)
+    roofline = {"bound": bound, "achieved": round(achieved, 1), "peak": round(peak, 1),
+                "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_source": (f"FP32-ALU bound: {SM_COUNT} SMs x {FP32_LANES_PER_SM} lanes x "
+                                f"{clk:.0f} MHz / {ALU_OPS_PER_ELEM} ops per element x "
+                                f"{BYTES_PER_ELEM} B per element (HBM bound: MEASURED_PEAKS.json "
+                                f"hbm_gbs {hbm_peak:.0f}, {peak_src})"),
                 "kernel": "quant_kernel (scale-sweep MSE, 11 candidates)",
                 "kernel_ms": round(q_ms, 4),
                 "algorithmic_bytes_per_launch": shard_bytes,
                 "traffic_source": traffic_src,
                 "alu": {"ops_per_elem": ALU_OPS_PER_ELEM, "sm_mhz": clk,
                         "peak_equiv_gbs": round(alu_peak_gbs, 1),
-                        "frac": round(achieved / alu_peak_gbs, 4),
-                        "note": "FP32-ALU roofline of the sweep: 148 SMs x 128 lanes x clock / "
-                                "35 ops per element, expressed in algorithmic GB/s"},
+                        "frac": round(achieved / alu_peak_gbs, 4)},
+                "hbm": {"peak_gbs": hbm_peak, "frac": round(achieved / hbm_peak, 4),
+                        "source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})"},
                 "amax_kernel_ms": round(amax_ms, 4),
                 "amax_achieved_gbs": round(rows * k * 2 / (amax_ms * 1e-3) / 1e9, 1)}
 
@@ -694,7 +827,42 @@ def run_ours(args):
                        "-> codes and scales to pinned host"}
         del h_in, h_codes, h_scales, x_dev
 
+    # whole-tensor bit-exactness against one GPU: every rank hashes its
+    # 16384-row chunks (codes + scale slab) and compares them with the
+    # committed digests of a one-GPU run of the same tensor
+    step()
+    torch.cuda.synchronize()
+    mine = chunk_digests(codes, scales, row0)
+    gsi_bits = int(gsi.view(torch.int32).item())
+    record = None
+    if os.path.exists(DIGEST_PATH):
+        with open(DIGEST_PATH) as f:
+            record = json.load(f)
+    comparable = (record is not None and record.get("rows") == args.rows and
+                  record.get("k") == k and record.get("chunk_rows") == CHUNK_ROWS)
+    ok = comparable and all(record["digests"].get(c) == d for c, d in mine.items()) and \
+        record.get("gsi_bits") == gsi_bits
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+    if world > 1:
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    bitexact = {"bitexact_vs_1gpu": bool(flag.item()) if comparable else None,
+                "chunks_checked": len(mine) * world, "chunk_rows": CHUNK_ROWS,
+                "record": os.path.relpath(DIGEST_PATH, ROOT) if comparable else
+                "no one-GPU record for this tensor size",
+                "gsi_bits": f"0x{gsi_bits & 0xFFFFFFFF:08X}"}
+    if args.write_config5_digests:
+        if world != 1:
+            raise SystemExit("--write-config5-digests is a one-GPU run")
+        with open(args.write_config5_digests, "w") as f:
+            json.dump({"rows": args.rows, "k": k, "chunk_rows": CHUNK_ROWS,
+                       "gsi_bits": gsi_bits, "digests": mine,
+                       "made_by": "python bench.py --no-sweep --no-gemm --no-cpu --no-e2e "
+                                  "--write-config5-digests <file> on one B200",
+                       "hash": "sha256 of each chunk's codes bytes then its scale slab bytes"},
+                      f, indent=1)
+
     sweep = None
+    ref_triton = None
     cpu = None
     gemm_res = None
     quality = None
@@ -705,6 +873,8 @@ def run_ours(args):
         torch.cuda.empty_cache()
         if not args.no_sweep:
             sweep = run_sweep(device)
+        if not args.no_ref_triton:
+            ref_triton = run_reference_triton_sweep(device)
         if not args.no_gemm:
             gemm_res = run_gemm_sweep(device)
         if not args.no_sweep:
@@ -726,11 +896,13 @@ def run_ours(args):
                            "step": "amax -> (NCCL MAX all-reduce if N>1) -> scale -> quantize"},
                 "gpu_launches": launches_per_step * args.steps,
                 "rank_ms_per_step": rank_ms,
-                "roofline": roofline, "clocks": clocks, "e2e": e2e}
+                "roofline": roofline, "clocks": clocks, "e2e": e2e, **bitexact}
         if cpu is not None:
             line["cpu_baseline"] = cpu
         if sweep is not None:
             line["sweep"] = sweep
+        if ref_triton is not None:
+            line["sweep_vs_reference_triton"] = ref_triton
         if quality is not None:
             line["quality_mse"] = quality
         if gemm_res is not None:

@@ -260,7 +260,11 @@ int ssw_nvfp4_quant_gemm(const void* x, int x_dtype, const float* x_scale, const
  *   - all calls share the scratch: calls that overlap on the GPU race, so
  *     order them on one stream;
  *   - the first call on a device looks up the scratch address for that
- *     device; make it before any stream capture.
+ *     device; make it before any stream capture;
+ *   - the address is cached per device for the process: do not call this
+ *     on a device again after cudaDeviceReset on it;
+ *   - a CUDA failure returns SSW_ERR_CUDA and ssw_last_error() names the
+ *     failing step and the CUDA error name.
  * Results equal ssw_global_scale_inv's bit for bit.
  */
 int64_t ssw_global_scale_inv_noalloc_max_numel(void);

@@ -31,9 +31,11 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import re
 import shutil
+import warnings
 
 import torch
 
@@ -82,8 +84,28 @@ def quantize_group(weights: list[torch.Tensor], weight_quantizer: str = "rtn"):
         if w.dim() != 2 or w.shape[1] % 16:
             raise ValueError(f"a weight must be 2-D with K % 16 == 0, got {tuple(w.shape)}")
     amax = torch.stack([absmax(w).reshape(()) for w in weights]).max().reshape(1)
-    gsi = scale_from_amax(amax, FP8_MAX)
+    gsi = scale_from_amax(amax, weight_fp8_max(weight_quantizer))
     return gsi, [quant(w, gsi, False) for w in weights]
+
+
+def weight_fp8_max(weight_quantizer: str) -> float:
+    """FP8 range behind a weight group's global scale: 448 for RTN, 256 for
+    the scale sweep, whose candidates above the base scale need E4M3 headroom
+    (the reference's convention for scale-sweep backends,
+    bench_kernel/test_kernel_latency.py:73-75)."""
+    from . import global_scale
+    if weight_quantizer not in ("rtn", "scalesweep_mse"):
+        raise ValueError(f"unknown weight quantizer {weight_quantizer!r}")
+    return global_scale.fp8_scale_max(weight_quantizer)
+
+
+def check_activation_amax(name: str, amax: float) -> float:
+    """An activation amax that gives a finite, nonzero input global scale."""
+    if not math.isfinite(amax) or amax <= 0.0:
+        raise ValueError(f"activation amax of {name} is {amax}: the input global scale "
+                         f"fp8_max*6/amax would not be finite and positive (a layer that saw "
+                         f"no calibration input, or inf/NaN activations)")
+    return amax
 
 
 def activation_scale(amax: float, device) -> torch.Tensor:
@@ -134,8 +156,11 @@ def calibrate(source: str, token_batches, *, targets: str = DEFAULT_TARGETS,
             running[name] = torch.zeros(1, dtype=torch.float32, device=device)
 
             def hook(module, args, name=name):
-                x = args[0].contiguous()
-                torch.maximum(running[name], global_scale.absmax(x), out=running[name])
+                x = args[0]
+                if x.numel() == 0:  # an empty batch carries no amax
+                    return
+                torch.maximum(running[name], global_scale.absmax(x.contiguous()),
+                              out=running[name])
             handles.append(mod.register_forward_pre_hook(hook))
     try:
         with torch.no_grad():
@@ -146,7 +171,12 @@ def calibrate(source: str, token_batches, *, targets: str = DEFAULT_TARGETS,
         for h in handles:
             h.remove()
     torch.cuda.synchronize()
-    return {name: float(v.item()) for name, v in running.items()}
+    result = {name: float(v.item()) for name, v in running.items()}
+    unseen = [n for n, v in result.items() if v == 0.0]
+    if unseen:
+        warnings.warn(f"{len(unseen)} target layers saw no nonzero calibration input "
+                      f"(amax 0), e.g. {unseen[0]}; quantize_checkpoint will reject them")
+    return result
 
 
 def quantize_checkpoint(source: str, destination: str, *, act_amax: float | dict = 16.0,
@@ -172,7 +202,8 @@ def quantize_checkpoint(source: str, destination: str, *, act_amax: float | dict
         gsi, results = quantize_group(ws, weight_quantizer)
         for name, (codes, scales) in zip(group, results):
             prefix = name[: -len(".weight")]
-            amax = act_amax[prefix] if isinstance(act_amax, dict) else act_amax
+            amax = check_activation_amax(
+                prefix, float(act_amax[prefix] if isinstance(act_amax, dict) else act_amax))
             out[prefix + ".weight_packed"] = codes.cpu()
             out[prefix + ".weight_scale"] = scales.cpu()
             out[prefix + ".weight_global_scale"] = gsi.cpu().clone()  # one tensor per name

@@ -26,8 +26,11 @@
 // it denotes a shadow object, not GPU memory.  The first call on each device,
 // with that device current, asks the runtime for the device address with
 // cudaGetSymbolAddress and caches it.  That first call should happen before
-// any stream capture begins.
+// any stream capture begins.  The cached address belongs to the device's
+// current context: after cudaDeviceReset on a device, this entry point must
+// not be called on it again in the same process.
 #include <cstdint>
+#include <cstdio>
 #include <mutex>
 
 #include <cuda_fp16.h>
@@ -114,21 +117,39 @@ __global__ void __launch_bounds__(kStaticThreads)
   }
 }
 
-// Device address of g_amax_scratch on the current device (set up once per device).
-cudaError_t scratch_for_current_device(uint32_t** out) {
+// Device address of g_amax_scratch on the current device (set up once per
+// device).  On failure *step names the call that failed.
+cudaError_t scratch_for_current_device(uint32_t** out, const char** step) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (e != cudaSuccess) {
+    *step = "cudaGetDevice";
+    return e;
+  }
+  if (dev < 0 || dev >= 64) {
+    *step = "device index >= 64 (the address cache holds 64 devices)";
+    return cudaErrorInvalidDevice;
+  }
   std::lock_guard<std::mutex> lock(g_setup_mutex);
   if (g_scratch_ptr[dev] == nullptr) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_amax_scratch);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) {
+      *step = "cudaGetSymbolAddress of the static scratch";
+      return e;
+    }
     g_scratch_ptr[dev] = static_cast<uint32_t*>(p);
   }
   *out = g_scratch_ptr[dev];
   return cudaSuccess;
+}
+
+// "<prefix><step> failed: <cudaErrorName> (<description>)" into the last-error slot.
+void report_cuda(const char* prefix, const char* step, cudaError_t e) {
+  char msg[320];
+  snprintf(msg, sizeof(msg), "%s%s failed: %s (%s)", prefix, step, cudaGetErrorName(e),
+           cudaGetErrorString(e));
+  ssw::set_last_error(msg);
 }
 
 }  // namespace
@@ -161,15 +182,16 @@ int ssw_global_scale_inv_noalloc(const void* input, int input_dtype, int64_t num
     return SSW_ERR_INVALID_ARGUMENT;
   }
   uint32_t* scratch = nullptr;
-  cudaError_t e = scratch_for_current_device(&scratch);
+  const char* step = nullptr;
+  cudaError_t e = scratch_for_current_device(&scratch, &step);
   if (e != cudaSuccess) {
-    ssw::set_last_error("global_scale_inv_noalloc: cudaGetSymbolAddress failed");
+    report_cuda("global_scale_inv_noalloc: ", step, e);
     return SSW_ERR_CUDA;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   e = cudaMemsetAsync(scratch + kTicketWord, 0, sizeof(uint32_t), s);
   if (e != cudaSuccess) {
-    ssw::set_last_error("global_scale_inv_noalloc: cudaMemsetAsync failed");
+    report_cuda("global_scale_inv_noalloc: ", "cudaMemsetAsync of the ticket", e);
     return SSW_ERR_CUDA;
   }
   const uint32_t grid = (uint32_t)(((uint64_t)numel + kStaticChunk - 1) / kStaticChunk);
@@ -179,7 +201,7 @@ int ssw_global_scale_inv_noalloc(const void* input, int input_dtype, int64_t num
                                                      fp8_max * 6.0f, input_scale_out, amax_out);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
-    ssw::set_last_error(cudaGetErrorString(e));
+    report_cuda("global_scale_inv_noalloc: ", "kernel launch", e);
     return SSW_ERR_CUDA;
   }
   return SSW_OK;

@@ -40,9 +40,20 @@ def scale_slab_rows(start: int, stop: int) -> tuple[int, int]:
 
 
 def all_reduce_amax(amax: torch.Tensor, group=None) -> torch.Tensor:
-    """In-place MAX all-reduce of the per-rank |x| maximum (float32 [1])."""
+    """In-place MAX all-reduce of the per-rank |x| maximum (float32 [1]).
+
+    The reduction runs on the float's bit pattern as int32.  An |x| maximum is
+    +0, a positive finite value, +inf or a NaN with the sign bit clear, and
+    for those patterns signed-integer order is value order with NaN above
+    +inf.  So the result is the largest amax, and a NaN on any rank wins, as
+    ``x.abs().max()`` over the whole tensor would give.  A float MAX would
+    not promise that: NCCL's and gloo's float maximum may drop a NaN operand.
+    """
+    if amax.dtype != torch.float32:
+        raise ValueError("amax must be float32")
     if dist.is_available() and dist.is_initialized():
-        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
+        bits = amax.view(torch.int32)
+        dist.all_reduce(bits, op=dist.ReduceOp.MAX, group=group)
     return amax
 
 

@@ -129,3 +129,37 @@ def test_calibration_refuses_without_a_gpu(tmp_path):
         pytest.skip("checks the no-GPU refusal")
     with pytest.raises(ValueError, match="CUDA"):
         checkpoint.calibrate(str(tmp_path), [[[1, 2, 3]]])
+
+
+def test_weight_global_scale_follows_the_quantizers_fp8_range(monkeypatch):
+    """RTN weights use fp8_max 448; scale-sweep weights 256, the reference's
+    convention for scale-sweep backends (headroom for the candidates above
+    the base scale)."""
+    assert checkpoint.weight_fp8_max("rtn") == 448.0
+    assert checkpoint.weight_fp8_max("scalesweep_mse") == 256.0
+    with pytest.raises(ValueError):
+        checkpoint.weight_fp8_max("cutlass")
+    seen = []
+
+    def absmax(w):
+        return torch.tensor([oracle.absmax(_bits(w))], dtype=torch.float32)
+
+    def scale_from_amax(amax, fp8_max):
+        seen.append(fp8_max)
+        return torch.tensor([oracle.global_scale_inv(float(amax.item()), fp8_max)],
+                            dtype=torch.float32)
+
+    monkeypatch.setattr(checkpoint, "_quantizers",
+                        lambda wq: (absmax, scale_from_amax, lambda w, g, s: (w, g)))
+    w = torch.full((16, 32), 2.0, dtype=torch.bfloat16)
+    for quantizer, fp8_max in (("rtn", 448.0), ("scalesweep_mse", 256.0)):
+        gsi, _ = checkpoint.quantize_group([w], quantizer)
+        assert seen[-1] == fp8_max
+        assert gsi.item() == np.float32(oracle.global_scale_inv(2.0, fp8_max))
+
+
+@pytest.mark.parametrize("amax", [0.0, float("inf"), float("nan"), -1.0])
+def test_activation_amax_must_give_a_finite_scale(amax):
+    with pytest.raises(ValueError, match="activation amax"):
+        checkpoint.check_activation_amax("model.layers.0.mlp.down_proj", amax)
+    assert checkpoint.check_activation_amax("x", 3.5) == 3.5

@@ -106,3 +106,41 @@ def test_missing_rank_surfaces_as_an_error_not_a_hang():
         p.join(timeout=90)
     assert all(p.exitcode is not None for p in procs), "a rank hung"
     assert procs[0].exitcode == 17
+
+
+def _amax_worker(rank, world, port, values, result_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    amax = torch.tensor([values[rank]], dtype=torch.float32)
+    sharded.all_reduce_amax(amax)
+    np.save(os.path.join(result_dir, f"a{rank}.npy"), amax.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("values,want", [
+    ((3.5, float("nan")), "nan"),          # NaN on the second rank
+    ((float("nan"), 1e30), "nan"),         # NaN on the first rank
+    ((float("inf"), 2.0), float("inf")),
+    ((0.0, 0.0), 0.0),
+    ((7.25, 1e-40), 7.25),                 # a subnormal amax loses to a normal one
+])
+def test_amax_all_reduce_carries_nan_and_inf(tmp_path, values, want):
+    """A NaN in any shard must make the tensor-wide amax NaN on every rank,
+    as x.abs().max() over the whole tensor does (the gsi then follows it)."""
+    port = _free_port()
+    mp.start_processes(_amax_worker, args=(2, port, values, str(tmp_path)), nprocs=2,
+                       start_method="spawn", join=True)
+    for r in range(2):
+        got = float(np.load(tmp_path / f"a{r}.npy")[0])
+        if want == "nan":
+            assert np.isnan(got), got
+        else:
+            assert got == want, got
+
+
+def test_amax_all_reduce_rejects_non_float32():
+    with pytest.raises(ValueError):
+        sharded.all_reduce_amax(torch.zeros(1, dtype=torch.float64))

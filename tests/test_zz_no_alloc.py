@@ -80,6 +80,51 @@ def test_no_alloc_matches_workspace_entry_on_two_calls_in_a_row(lib, shape, dtyp
         assert m_got.item() == x.abs().max().float().item()
 
 
+def _same(a, b):
+    return _bits(a) == _bits(b)
+
+
+def _check_pair(lib, x, fp8_max):
+    s_ref, m_ref = _with_workspace(lib, x, fp8_max)
+    s_got, m_got = _no_alloc(lib, x, fp8_max)
+    torch.cuda.synchronize()
+    assert _same(s_got, s_ref), (s_got.item(), s_ref.item())
+    assert _same(m_got, m_ref), (m_got.item(), m_ref.item())
+    return m_got.item()
+
+
+def test_no_alloc_partial_tail_chunk_and_specials_in_a_late_chunk(lib):
+    """3001 x 4096 elements end 0.1 of the way into a 32768-element chunk
+    (the aligned path with a partial last CTA).  Then a NaN, an Inf and an
+    all-zero tensor, each placed where only a late CTA sees it."""
+    g = torch.Generator(device="cuda").manual_seed(3001)
+    x = torch.randn(3001, 4096, generator=g, device="cuda").to(torch.bfloat16)
+    assert x.numel() % 32768 != 0
+    assert _check_pair(lib, x, 448.0) == x.abs().max().float().item()
+    x_nan = x.clone()
+    x_nan.view(-1)[x.numel() - 5] = float("nan")
+    assert torch.isnan(torch.tensor(_check_pair(lib, x_nan, 448.0)))
+    x_inf = x.clone()
+    x_inf.view(-1)[x.numel() - 40000] = float("-inf")
+    assert _check_pair(lib, x_inf, 256.0) == float("inf")
+    zeros = torch.zeros(3001, 4096, dtype=torch.bfloat16, device="cuda")
+    assert _check_pair(lib, zeros, 448.0) == 0.0   # the scale is then 1/0 = inf in both
+
+
+def test_no_alloc_at_its_size_limit(lib):
+    """Exactly the largest size the static scratch allows, and one chunk less."""
+    limit = lib.ssw_global_scale_inv_noalloc_max_numel()
+    g = torch.Generator(device="cuda").manual_seed(28)
+    x = torch.empty(limit, dtype=torch.bfloat16, device="cuda")
+    for i in range(0, limit, 1 << 26):
+        x[i:i + (1 << 26)] = torch.randn(1 << 26, generator=g, device="cuda")
+    x[limit - 3] = 1000.0  # the maximum sits in the very last CTA
+    assert _check_pair(lib, x, 448.0) == 1000.0
+    assert _check_pair(lib, x[: limit - 32768], 448.0) == x[: limit - 32768].abs().max().item()
+    del x
+    torch.cuda.empty_cache()
+
+
 def test_no_alloc_rejects_tensors_beyond_its_static_scratch(lib):
     limit = lib.ssw_global_scale_inv_noalloc_max_numel()
     assert limit == 1 << 28
