@@ -47,6 +47,22 @@ SWEEP_K = (4096, 8192, 14336)
 ALU_OPS_PER_ELEM = 35  # sweep's FP32 op count per element (roofline definition)
 SM_COUNT = 148
 FP32_LANES_PER_SM = 128
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+# vLLM end-to-end arms: the backend passed to vllm_e2e.run, and whether the
+# activation quantizer is the reference's own Triton kernel
+VLLM_ARMS = {
+    "cutlass": "vLLM's own RTN activation quantizer (CUTLASS path)",
+    "reference_triton": "the reference's Triton scalesweep_mse kernel "
+                        "(bench_kernel/scalesweep_mse_nvfp4_utils.py:498-519), registered as "
+                        "torch.ops.vllm.scalesweep_mse_nvfp4_quant with its own fake "
+                        "implementation (:546-560), SCALESWEEP_TUNE=0 as in run_bench_tune.sh",
+    "scalesweep_mse": "this package's scalesweep_mse quantizer",
+    "scalesweep_mse_fused_norm_act": "this package's quantizer with RMSNorm and SiLU-and-mul fused "
+                                     "into it",
+}
+# (input tokens, output tokens, batch sizes): config 4, and the reference's
+# own 256-request run (benchmark_nvfp4_tokens.py defaults, run_bench_tune.sh)
+VLLM_WORKLOADS = {"decode": (1024, 256, (1, 16, 64, 256)), "reference": (2048, 256, (256,))}
 
 
 def parse_args():
@@ -80,6 +96,15 @@ def parse_args():
     ap.add_argument("--profile-norm", default=None, metavar="MxN",
                     help="only run the RMSNorm-fused quantizer (plain, then with a residual) "
                          "on an [M, N] input 4 times each and exit (for ncu)")
+    ap.add_argument("--vllm-e2e", action="store_true",
+                    help="Llama-3.1-8B W4A4 in vLLM on one GPU: output tok/s of each arm "
+                         "(--vllm-arms), one engine process per run, arms interleaved over "
+                         "--vllm-repeats rounds; prints one JSON line and exits")
+    ap.add_argument("--vllm-arms", nargs="+", default=list(VLLM_ARMS), choices=list(VLLM_ARMS))
+    ap.add_argument("--vllm-repeats", type=int, default=3)
+    ap.add_argument("--vllm-workload", choices=sorted(VLLM_WORKLOADS), default="decode")
+    ap.add_argument("--vllm-arm", default=None, choices=list(VLLM_ARMS),
+                    help=argparse.SUPPRESS)  # one engine run (a child of --vllm-e2e)
     return ap.parse_args()
 
 
@@ -353,7 +378,6 @@ def run_sweep(device, reps: int = 20):
     return out
 
 
-REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
 
 def load_reference_dispatcher():
@@ -997,8 +1021,94 @@ def run_profile_norm(args):
     print(json.dumps({"profile_norm": [m, n]}))
 
 
+def register_reference_quant_op():
+    """The reference's Triton ``scalesweep_mse_nvfp4_quant_impl`` as a torch op,
+    registered the way the reference's vLLM fork registers it (the names in
+    test_kernel_latency.py:41-47; its fake implementation
+    bench_kernel/scalesweep_mse_nvfp4_utils.py:546-560), from the unmodified
+    install under baseline/_ref.  SCALESWEEP_TUNE=0: one kernel configuration,
+    as run_bench_tune.sh exports for its end-to-end runs."""
+    import torch
+    os.environ["SCALESWEEP_TUNE"] = "0"
+    if not os.path.isdir(os.path.join(REF_DIR, "bench_kernel")):
+        raise SystemExit("reference not installed under baseline/_ref "
+                         "(python baseline/install_ref.py)")
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    from bench_kernel import scalesweep_mse_nvfp4_utils as k1
+    from vllm.utils.torch_utils import direct_register_custom_op
+    direct_register_custom_op("scalesweep_mse_nvfp4_quant", k1.scalesweep_mse_nvfp4_quant_impl,
+                              mutates_args=[], fake_impl=k1._scalesweep_mse_nvfp4_quant_fake)
+    return torch.ops.vllm.scalesweep_mse_nvfp4_quant
+
+
+def run_vllm_arm(args):
+    """One vLLM engine with one arm; prints its result as one JSON line."""
+    from test_speed_scalesweep_b200 import vllm_e2e
+    input_len, output_len, batches = VLLM_WORKLOADS[args.vllm_workload]
+    arm = args.vllm_arm
+    if arm == "reference_triton":
+        res = vllm_e2e.run("cutlass", batches, input_len, output_len,
+                           quant_op=register_reference_quant_op())
+    else:
+        res = vllm_e2e.run(arm, batches, input_len, output_len)
+    res["arm"] = arm
+    print("VLLM_ARM_RESULT " + json.dumps(res), flush=True)
+
+
+def run_vllm_e2e(args):
+    """Arms interleaved over repeats (arm order rotated each round), one engine
+    process per run; per batch size the mean, min and max output tok/s of
+    each arm, and each arm's mean over the reference Triton arm's mean."""
+    input_len, output_len, batches = VLLM_WORKLOADS[args.vllm_workload]
+    arms = list(args.vllm_arms)
+    runs = {a: [] for a in arms}
+    failures = []
+    for r in range(args.vllm_repeats):
+        order = arms[r % len(arms):] + arms[:r % len(arms)]
+        for arm in order:
+            cmd = [sys.executable, os.path.abspath(__file__), "--vllm-arm", arm,
+                   "--vllm-workload", args.vllm_workload]
+            env = dict(os.environ, VLLM_ENABLE_V1_MULTIPROCESSING="0")
+            t0 = time.time()
+            proc = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=1800)
+            line = [ln for ln in proc.stdout.splitlines() if ln.startswith("VLLM_ARM_RESULT ")]
+            if proc.returncode != 0 or not line:
+                failures.append({"arm": arm, "repeat": r, "rc": proc.returncode,
+                                 "tail": (proc.stdout + proc.stderr)[-800:]})
+                continue
+            res = json.loads(line[-1][len("VLLM_ARM_RESULT "):])
+            res["process_seconds"] = round(time.time() - t0, 1)
+            runs[arm].append(res)
+    out = {"vllm_e2e": f"Llama-3.1-8B architecture W4A4 in vLLM, one B200, {input_len} in / "
+                       f"{output_len} out, CUDA graphs, fusion passes off",
+           "workload": args.vllm_workload, "repeats": args.vllm_repeats,
+           "order": "arms interleaved, order rotated each repeat; one engine process per run",
+           "arms": {a: VLLM_ARMS[a] for a in arms}, "batch": {}, "failures": failures}
+    for bs in batches:
+        row = {}
+        for arm in arms:
+            vals = [r["batch"][str(bs)]["output_tok_s"] for r in runs[arm]]
+            if vals:
+                row[arm] = {"mean": round(statistics.mean(vals), 2), "min": min(vals),
+                            "max": max(vals), "runs": vals}
+        ref = row.get("reference_triton", {}).get("mean")
+        if ref:
+            for arm in arms:
+                if arm in row:
+                    row[arm]["over_reference_triton"] = round(row[arm]["mean"] / ref, 4)
+        out["batch"][str(bs)] = row
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.vllm_arm:
+        run_vllm_arm(args)
+        return
+    if args.vllm_e2e:
+        run_vllm_e2e(args)
+        return
     if args.profile_case:
         run_profile_case(args)
         return

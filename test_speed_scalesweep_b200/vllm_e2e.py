@@ -107,16 +107,20 @@ def write_model_dir(path: str) -> str:
 HOOK_CALLS = {"count": 0}
 
 
-def install_act_quant_hook(backend: str) -> int:
+def install_act_quant_hook(backend: str, op=None) -> int:
     """Route vLLM's W4A4 activation quantization through this package's kernels.
 
     Every vLLM module that imported ``scaled_fp4_quant`` by name (the CUTLASS
     and FlashInfer NVFP4 linear kernels among them) gets the replacement, so
     the hook holds whichever linear backend vLLM picks.  ``backend="cutlass"``
-    leaves vLLM's own quantizer in place (the baseline).  Returns the number
-    of module-level names rebound.
+    leaves vLLM's own quantizer in place (the baseline).  ``op``, when given,
+    replaces this package's op: any registered op with the signature
+    ``op(x2d, input_global_scale, is_sf_swizzled_layout, padded_n) ->
+    (codes, scales)``, such as another implementation of the same quantizer
+    timed under the same hook.  Returns the number of module-level names
+    rebound.
     """
-    if backend == "cutlass":
+    if backend == "cutlass" and op is None:
         return 0
     import importlib
     import sys
@@ -131,7 +135,8 @@ def install_act_quant_hook(backend: str) -> int:
         except Exception:  # pragma: no cover - depends on the vLLM build
             pass
     original = vllm_ops.scaled_fp4_quant
-    op = getattr(torch.ops.scalesweep_b200, _OP_FOR_BACKEND[backend])
+    if op is None:
+        op = getattr(torch.ops.scalesweep_b200, _OP_FOR_BACKEND[backend])
 
     def scaled_fp4_quant(input, input_global_scale, is_sf_swizzled_layout=True,
                          backend="none", padded_n=None):
@@ -371,12 +376,19 @@ def init_random_nvfp4_weights(model: torch.nn.Module, act_amax: float = 16.0,
 
 
 def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 0,
-        gpu_memory_utilization: float = 0.85, enforce_eager: bool = False) -> dict:
+        gpu_memory_utilization: float = 0.85, enforce_eager: bool = False,
+        quant_op=None) -> dict:
+    """One vLLM engine, one backend: output tok/s for each batch size.
+
+    ``quant_op`` (with ``backend="cutlass"``) installs another registered
+    activation quantizer under the same hook, so two implementations of the
+    quantizer are timed through the same integration."""
     os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
     linear_ours = backend == "scalesweep_mse_linear"
     fused_norm = backend == "scalesweep_mse_fused_norm_act"
     fused_act = backend == "scalesweep_mse_fused_act" or fused_norm
-    rebound = install_act_quant_hook("scalesweep_mse" if (linear_ours or fused_act) else backend)
+    rebound = install_act_quant_hook("scalesweep_mse" if (linear_ours or fused_act) else backend,
+                                     op=quant_op)
     if linear_ours:
         install_linear_hook()
     if fused_act:
