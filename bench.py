@@ -58,7 +58,9 @@ VLLM_ARMS = {
                         "implementation (:546-560), SCALESWEEP_TUNE=0 as in run_bench_tune.sh",
     "scalesweep_mse": "this package's scalesweep_mse quantizer",
     "scalesweep_mse_fused_norm_act": "this package's quantizer with RMSNorm and SiLU-and-mul fused "
-                                     "into it",
+                                     "into it (Llama module hooks)",
+    "scalesweep_mse_fusion_pass": "the same fusions reached through a vLLM compile pass "
+                                  "(vllm_fusion.py) instead of module hooks",
 }
 # (input tokens, output tokens, batch sizes): config 4, and the reference's
 # own 256-request run (benchmark_nvfp4_tokens.py defaults, run_bench_tune.sh)

@@ -87,9 +87,12 @@ NVFP4_QUANT_CONFIG = {
 # "scalesweep_mse_fused_norm_act": also each decoder layer's two RMSNorms are
 # fused into the qkv and gate_up projections' quantizers
 # (install_fused_norm_hook).
+# "scalesweep_mse_fusion_pass": the same fusions as scalesweep_mse_fused_norm_act,
+# reached through vLLM's compile passes instead of module hooks
+# (vllm_fusion.install_fusion_pass), so they apply to any model's graph.
 BACKENDS = ("scalesweep_mse", "scalesweep_mse_reference", "rtn", "cutlass",
             "scalesweep_mse_linear", "scalesweep_mse_fused_act",
-            "scalesweep_mse_fused_norm_act")
+            "scalesweep_mse_fused_norm_act", "scalesweep_mse_fusion_pass")
 _OP_FOR_BACKEND = {"scalesweep_mse": "scalesweep_mse_nvfp4_quant",
                    "scalesweep_mse_reference": "scalesweep_mse_reference_nvfp4_quant",
                    "rtn": "rtn_nvfp4_quant"}
@@ -141,7 +144,9 @@ def install_act_quant_hook(backend: str, op=None) -> int:
     def scaled_fp4_quant(input, input_global_scale, is_sf_swizzled_layout=True,
                          backend="none", padded_n=None):
         HOOK_CALLS["count"] += 1
-        x = input.reshape(-1, input.shape[-1])
+        # no view node for the usual 2-D input, so a fusion pass sees the
+        # producer feed the quantizer directly
+        x = input if input.dim() == 2 else input.reshape(-1, input.shape[-1])
         if padded_n is not None and padded_n == x.shape[-1]:
             padded_n = None
         return op(x, input_global_scale, is_sf_swizzled_layout, padded_n)
@@ -387,8 +392,12 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
     linear_ours = backend == "scalesweep_mse_linear"
     fused_norm = backend == "scalesweep_mse_fused_norm_act"
     fused_act = backend == "scalesweep_mse_fused_act" or fused_norm
-    rebound = install_act_quant_hook("scalesweep_mse" if (linear_ours or fused_act) else backend,
-                                     op=quant_op)
+    fusion_pass = backend == "scalesweep_mse_fusion_pass"
+    rebound = install_act_quant_hook(
+        "scalesweep_mse" if (linear_ours or fused_act or fusion_pass) else backend, op=quant_op)
+    if fusion_pass:
+        from . import vllm_fusion
+        vllm_fusion.install_fusion_pass()
     if linear_ours:
         install_linear_hook()
     if fused_act:
@@ -446,6 +455,10 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
     if fused_act:
         results["mlp_hook_calls"] = dict(MLP_CALLS)
         results["fusion"] = "SiLU-and-mul + scale-sweep quant fused (this package)"
+    if fusion_pass:
+        results["fusion_pass_matches"] = dict(vllm_fusion.MATCHES)
+        results["fusion"] = ("RMSNorm / fused-add RMSNorm / SiLU-and-mul + scale-sweep quant "
+                             "fused by a vLLM compile pass (this package)")
     if fused_norm:
         results["decoder_hook_calls"] = dict(DECODER_CALLS)
         results["fusion"] = ("RMSNorm + scale-sweep quant (qkv, gate_up) and SiLU-and-mul + "
