@@ -61,6 +61,11 @@ VLLM_ARMS = {
                                      "into it (Llama module hooks)",
     "scalesweep_mse_fusion_pass": "the same fusions reached through a vLLM compile pass "
                                   "(vllm_fusion.py) instead of module hooks",
+    "scalesweep_mse_dispatch": "this package's quantizer; each linear layer's GEMM from this "
+                               "package (quantizer + GEMM in one call) at token counts where it "
+                               "is faster, vLLM's CUTLASS GEMM elsewhere",
+    "scalesweep_mse_fused_norm_act_dispatch": "the fused RMSNorm/SiLU-and-mul hooks with the "
+                                              "same per-call GEMM choice",
 }
 # (input tokens, output tokens, batch sizes): config 4, and the reference's
 # own 256-request run (benchmark_nvfp4_tokens.py defaults, run_bench_tune.sh)
@@ -105,6 +110,9 @@ def parse_args():
     ap.add_argument("--vllm-arms", nargs="+", default=list(VLLM_ARMS), choices=list(VLLM_ARMS))
     ap.add_argument("--vllm-repeats", type=int, default=3)
     ap.add_argument("--vllm-workload", choices=sorted(VLLM_WORKLOADS), default="decode")
+    ap.add_argument("--gemm-crossover", action="store_true",
+                    help="time the whole linear layer from this package against the quantizer "
+                         "+ vLLM's GEMM over token counts; prints one JSON line and exits")
     ap.add_argument("--vllm-arm", default=None, choices=list(VLLM_ARMS),
                     help=argparse.SUPPRESS)  # one engine run (a child of --vllm-e2e)
     return ap.parse_args()
@@ -606,6 +614,51 @@ def run_gemm_sweep(device, reps: int = 20):
             del x, qa, sa
         del qb, sb
     return out
+
+
+CROSSOVER_M = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256, 384, 512, 1024, 2048, 8192)
+
+
+def run_gemm_crossover(args):
+    """Where the whole linear layer from this package (scale-sweep quantizer,
+    then this GEMM as its programmatic dependent) beats scale-sweep
+    quantization followed by vLLM's CUTLASS NVFP4 GEMM, per Llama-3.1-8B
+    shape and token count M.  Prints one JSON line."""
+    import torch
+    import vllm._custom_ops as vops
+    from test_speed_scalesweep_b200 import global_scale
+    from test_speed_scalesweep_b200 import scalesweep_mse_nvfp4_utils as mse
+    from test_speed_scalesweep_b200.gemm import scalesweep_nvfp4_linear
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    out = {"gemm_crossover": "per-launch us, one CUDA graph of 20 launches; 'ours' = "
+                             "scalesweep_nvfp4_linear (quantizer + this GEMM, one call), "
+                             "'vllm' = scale-sweep quantizer + vLLM cutlass_scaled_fp4_mm",
+           "shapes": {}}
+    for k, n in GEMM_SHAPES:
+        g = torch.Generator(device=device).manual_seed(k + n)
+        w = (torch.randn(n, k, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        w_gsi = global_scale.global_scale_inv_from_max(w, FP8_MAX)
+        qb, sb = mse.rtn_nvfp4_quant_impl(w, w_gsi, True)
+        del w
+        rows = {}
+        for m in CROSSOVER_M:
+            x = make_shard(m, k, 3 + m + k, device)
+            a_gsi = global_scale.global_scale_inv_from_max(x, FP8_MAX)
+            alpha = (1.0 / (a_gsi * w_gsi)).reshape(1).float()
+
+            def vllm_path():
+                ca, csa = mse.scalesweep_mse_nvfp4_quant_impl(x, a_gsi, True)
+                return vops.cutlass_scaled_fp4_mm(ca, qb, csa, sb, alpha, torch.bfloat16)
+            ours = graph_avg_ms(lambda: scalesweep_nvfp4_linear(x, a_gsi, qb, sb, alpha), 20,
+                                device)
+            theirs = graph_avg_ms(vllm_path, 20, device)
+            rows[str(m)] = {"ours_us": round(ours * 1e3, 2), "vllm_us": round(theirs * 1e3, 2),
+                            "vllm_over_ours": round(theirs / ours, 3)}
+            del x
+        out["shapes"][f"K{k}_N{n}"] = rows
+        del qb, sb
+    print(json.dumps(out), flush=True)
 
 
 def cpu_sample_rate(rows_hint: int, budget_s: float = 12.0):
@@ -1110,6 +1163,9 @@ def main():
         return
     if args.vllm_e2e:
         run_vllm_e2e(args)
+        return
+    if args.gemm_crossover:
+        run_gemm_crossover(args)
         return
     if args.profile_case:
         run_profile_case(args)

@@ -90,9 +90,13 @@ NVFP4_QUANT_CONFIG = {
 # "scalesweep_mse_fusion_pass": the same fusions as scalesweep_mse_fused_norm_act,
 # reached through vLLM's compile passes instead of module hooks
 # (vllm_fusion.install_fusion_pass), so they apply to any model's graph.
+# "..._dispatch": as without the suffix, but each GEMM (with its quantizer,
+# where the hook issues both) is this package's where it is faster than vLLM's
+# at the call's token count (OURS_UP_TO_M), vLLM's elsewhere.
 BACKENDS = ("scalesweep_mse", "scalesweep_mse_reference", "rtn", "cutlass",
             "scalesweep_mse_linear", "scalesweep_mse_fused_act",
-            "scalesweep_mse_fused_norm_act", "scalesweep_mse_fusion_pass")
+            "scalesweep_mse_fused_norm_act", "scalesweep_mse_fusion_pass",
+            "scalesweep_mse_dispatch", "scalesweep_mse_fused_norm_act_dispatch")
 _OP_FOR_BACKEND = {"scalesweep_mse": "scalesweep_mse_nvfp4_quant",
                    "scalesweep_mse_reference": "scalesweep_mse_reference_nvfp4_quant",
                    "rtn": "rtn_nvfp4_quant"}
@@ -161,9 +165,81 @@ def install_act_quant_hook(backend: str, op=None) -> int:
 
 LINEAR_CALLS = {"ours": 0, "fallback": 0}
 
+# Largest token count M at which this package's GEMM (with the quantizer as
+# its programmatic dependent launch, for the whole linear layer) beats vLLM's
+# CUTLASS NVFP4 GEMM, per Llama-3.1-8B shape (K, N); measured on B200 with
+# ``python bench.py --gemm-crossover``.  Larger M, and shapes not listed, use
+# vLLM's GEMM.
+OURS_UP_TO_M = {}
+GEMM_DISPATCH = {"on": False, "ours": 0, "vllm": 0}
 
-def install_linear_hook() -> None:
-    """Route vLLM's W4A4 linear layer through ``scalesweep_nvfp4_linear``.
+
+def _ours_for(m: int, n: int, k: int) -> bool:
+    return m <= OURS_UP_TO_M.get((k, n), 0) and k % 256 == 0 and n % 128 == 0
+
+
+_DISPATCH_LIB = None
+
+
+def register_dispatch_ops() -> None:
+    """``scalesweep_b200::nvfp4_mm_dispatch`` and
+    ``scalesweep_b200::scalesweep_nvfp4_linear_dispatch``: the GEMM, or the
+    whole W4A4 linear layer, from this package where it is faster
+    (``OURS_UP_TO_M``) and from vLLM's CUTLASS kernel elsewhere.  The choice
+    is made at run time from the actual token count, inside an op that
+    torch.compile treats as opaque, so one compiled graph serves every M.
+    Idempotent."""
+    global _DISPATCH_LIB
+    if _DISPATCH_LIB is not None:
+        return
+    import vllm._custom_ops as vllm_ops
+
+    from . import ops  # noqa: F401  (registers torch.ops.scalesweep_b200.*)
+    from .gemm import cutlass_scaled_fp4_mm, scalesweep_nvfp4_linear
+    from .scalesweep_mse_nvfp4_utils import scalesweep_mse_nvfp4_quant_impl
+
+    lib = torch.library.Library("scalesweep_b200", "FRAGMENT")
+    lib.define("nvfp4_mm_dispatch(Tensor a, Tensor b, Tensor a_scale, Tensor b_scale, "
+               "Tensor alpha) -> Tensor")
+    lib.define("scalesweep_nvfp4_linear_dispatch(Tensor x, Tensor input_scale, Tensor weight, "
+               "Tensor weight_scale, Tensor alpha) -> Tensor")
+
+    def mm(a, b, a_scale, b_scale, alpha):
+        m, n, k = a.shape[0], b.shape[0], a.shape[1] * 2
+        if _ours_for(m, n, k):
+            GEMM_DISPATCH["ours"] += 1
+            return cutlass_scaled_fp4_mm(a, b, a_scale, b_scale, alpha)
+        GEMM_DISPATCH["vllm"] += 1
+        return vllm_ops.cutlass_scaled_fp4_mm(a, b, a_scale, b_scale, alpha, torch.bfloat16)
+
+    def linear(x, input_scale, weight, weight_scale, alpha):
+        m, k, n = x.shape[0], x.shape[1], weight.shape[0]
+        if _ours_for(m, n, k) and x.dtype == torch.bfloat16:
+            GEMM_DISPATCH["ours"] += 1
+            return scalesweep_nvfp4_linear(x, input_scale, weight, weight_scale, alpha)
+        GEMM_DISPATCH["vllm"] += 1
+        codes, scales = scalesweep_mse_nvfp4_quant_impl(x, input_scale, True)
+        return vllm_ops.cutlass_scaled_fp4_mm(codes, weight, scales, weight_scale, alpha,
+                                              x.dtype)
+
+    def fake_mm(a, b, a_scale, b_scale, alpha):
+        return a.new_empty((a.shape[0], b.shape[0]), dtype=torch.bfloat16)
+
+    def fake_linear(x, input_scale, weight, weight_scale, alpha):
+        return x.new_empty((x.shape[0], weight.shape[0]))
+
+    lib.impl("nvfp4_mm_dispatch", mm, "CUDA")
+    lib.impl("scalesweep_nvfp4_linear_dispatch", linear, "CUDA")
+    torch.library.register_fake("scalesweep_b200::nvfp4_mm_dispatch", fake_mm, lib=lib)
+    torch.library.register_fake("scalesweep_b200::scalesweep_nvfp4_linear_dispatch", fake_linear,
+                                lib=lib)
+    _DISPATCH_LIB = lib
+
+
+def install_linear_hook(dispatch: bool = False) -> None:
+    """Route vLLM's W4A4 linear layer through ``scalesweep_nvfp4_linear``
+    (with ``dispatch``: through ``scalesweep_nvfp4_linear_dispatch``, which
+    keeps vLLM's GEMM where it is the faster one).
 
     ``CutlassNvFp4LinearKernel.apply_weights`` (vllm 0.22
     ``model_executor/kernels/linear/nvfp4/cutlass.py:45-77``) calls
@@ -180,6 +256,10 @@ def install_linear_hook() -> None:
     original = CutlassNvFp4LinearKernel.apply_weights
     if getattr(original, "_scalesweep_b200", False):
         return
+    if dispatch:
+        register_dispatch_ops()
+    linear_op = (torch.ops.scalesweep_b200.scalesweep_nvfp4_linear_dispatch if dispatch
+                 else torch.ops.scalesweep_b200.scalesweep_nvfp4_linear)
 
     def apply_weights(self, layer, x, bias=None):
         k = x.shape[-1]
@@ -189,9 +269,8 @@ def install_linear_hook() -> None:
             LINEAR_CALLS["fallback"] += 1
             return original(self, layer, x, bias)
         LINEAR_CALLS["ours"] += 1
-        out = torch.ops.scalesweep_b200.scalesweep_nvfp4_linear(
-            x.reshape(-1, k), layer.input_global_scale_inv, layer.weight, layer.weight_scale,
-            layer.alpha)
+        out = linear_op(x.reshape(-1, k), layer.input_global_scale_inv, layer.weight,
+                        layer.weight_scale, layer.alpha)
         output_size = layer.output_size_per_partition
         if n != output_size:
             out = out[:, :output_size]
@@ -252,8 +331,12 @@ def _fp4_linear(lin, codes, scales, lead_shape, dtype):
     ``CutlassNvFp4LinearKernel.apply_weights`` runs it after quantizing
     (vllm 0.22 ``model_executor/kernels/linear/nvfp4/cutlass.py:64-77``)."""
     import vllm._custom_ops as vllm_ops
-    out = vllm_ops.cutlass_scaled_fp4_mm(codes, lin.weight, scales, lin.weight_scale, lin.alpha,
-                                         dtype)
+    if GEMM_DISPATCH["on"] and dtype == torch.bfloat16:
+        out = torch.ops.scalesweep_b200.nvfp4_mm_dispatch(codes, lin.weight, scales,
+                                                          lin.weight_scale, lin.alpha)
+    else:
+        out = vllm_ops.cutlass_scaled_fp4_mm(codes, lin.weight, scales, lin.weight_scale,
+                                             lin.alpha, dtype)
     out = out[:, :lin.output_size_per_partition]
     if lin.bias is not None:
         out = out + lin.bias
@@ -389,12 +472,19 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
     activation quantizer under the same hook, so two implementations of the
     quantizer are timed through the same integration."""
     os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
+    dispatch = backend.endswith("_dispatch")
+    if dispatch:
+        backend = backend[: -len("_dispatch")]
     linear_ours = backend == "scalesweep_mse_linear"
     fused_norm = backend == "scalesweep_mse_fused_norm_act"
     fused_act = backend == "scalesweep_mse_fused_act" or fused_norm
     fusion_pass = backend == "scalesweep_mse_fusion_pass"
     rebound = install_act_quant_hook(
         "scalesweep_mse" if (linear_ours or fused_act or fusion_pass) else backend, op=quant_op)
+    if dispatch:
+        register_dispatch_ops()
+        GEMM_DISPATCH["on"] = True
+        install_linear_hook(dispatch=True)
     if fusion_pass:
         from . import vllm_fusion
         vllm_fusion.install_fusion_pass()
@@ -425,7 +515,8 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
     gen = torch.Generator().manual_seed(seed)
     params = SamplingParams(max_tokens=output_len, ignore_eos=True, temperature=1.0,
                             detokenize=False, seed=seed)
-    results = {"backend": backend, "input_len": input_len, "output_len": output_len,
+    results = {"backend": backend + ("_dispatch" if dispatch else ""),
+               "input_len": input_len, "output_len": output_len,
                "quantized_layers": n_layers, "hook_rebound_names": rebound, "batch": {},
                "linear_backend": ("scalesweep_b200 quantizer + GEMM (one op)" if linear_ours
                                   else "vLLM CUTLASS"), "fusion": "off",
@@ -455,6 +546,11 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
     if fused_act:
         results["mlp_hook_calls"] = dict(MLP_CALLS)
         results["fusion"] = "SiLU-and-mul + scale-sweep quant fused (this package)"
+    if dispatch:
+        results["gemm_dispatch_calls"] = {"ours": GEMM_DISPATCH["ours"],
+                                          "vllm": GEMM_DISPATCH["vllm"]}
+        results["linear_backend"] = ("this package's GEMM up to OURS_UP_TO_M tokens, "
+                                     "vLLM CUTLASS above")
     if fusion_pass:
         results["fusion_pass_matches"] = dict(vllm_fusion.MATCHES)
         results["fusion"] = ("RMSNorm / fused-add RMSNorm / SiLU-and-mul + scale-sweep quant "

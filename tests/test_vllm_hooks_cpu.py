@@ -115,3 +115,34 @@ def test_fused_norm_hook_feeds_each_norm_to_the_next_projections_quantizer(monke
     mlp.down_proj.tp_size = 2                                # tensor parallel: vLLM's path
     assert fwd(layer, pos, x, res2) == "vllm"
     assert vllm_e2e.DECODER_CALLS == {"fused": 2, "fallback": 1}
+
+
+def test_gemm_dispatch_rule_and_shapes(monkeypatch):
+    vllm_e2e.register_dispatch_ops()
+    monkeypatch.setattr(vllm_e2e, "OURS_UP_TO_M", {(4096, 28672): 64})
+    assert vllm_e2e._ours_for(64, 28672, 4096)
+    assert not vllm_e2e._ours_for(65, 28672, 4096)       # above the measured crossover
+    assert not vllm_e2e._ours_for(16, 6144, 4096)        # shape not listed: vLLM's GEMM
+    monkeypatch.setattr(vllm_e2e, "OURS_UP_TO_M", {(4000, 28672): 64})
+    assert not vllm_e2e._ours_for(16, 28672, 4000)       # K the GEMM does not take
+    meta = dict(device="meta")
+    a = torch.empty(16, 2048, dtype=torch.uint8, **meta)
+    b = torch.empty(28672, 2048, dtype=torch.uint8, **meta)
+    sa = torch.empty(128, 256, dtype=torch.float8_e4m3fn, **meta)
+    sb = torch.empty(28672, 256, dtype=torch.float8_e4m3fn, **meta)
+    alpha = torch.empty(1, **meta)
+    out = torch.ops.scalesweep_b200.nvfp4_mm_dispatch(a, b, sa, sb, alpha)
+    assert out.shape == (16, 28672) and out.dtype == torch.bfloat16
+    x = torch.empty(16, 4096, dtype=torch.bfloat16, **meta)
+    out = torch.ops.scalesweep_b200.scalesweep_nvfp4_linear_dispatch(x, alpha, b, sb, alpha)
+    assert out.shape == (16, 28672) and out.dtype == torch.bfloat16
+
+
+def test_linear_hook_with_dispatch_calls_the_dispatch_op(monkeypatch):
+    monkeypatch.setattr(vllm_cutlass.CutlassNvFp4LinearKernel, "apply_weights",
+                        lambda self, layer, x, bias=None: "vllm")
+    vllm_e2e.install_linear_hook(dispatch=True)
+    apply = vllm_cutlass.CutlassNvFp4LinearKernel.apply_weights
+    x = torch.empty(3, 4096, dtype=torch.bfloat16, device="meta")
+    out = apply(None, _layer(n=4096), x)
+    assert out.shape == (3, 4096)
