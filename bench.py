@@ -1118,6 +1118,7 @@ def run_vllm_e2e(args):
     input_len, output_len, batches = VLLM_WORKLOADS[args.vllm_workload]
     arms = list(args.vllm_arms)
     runs = {a: [] for a in arms}
+    meta = {}
     failures = []
     for r in range(args.vllm_repeats):
         order = arms[r % len(arms):] + arms[:r % len(arms)]
@@ -1135,11 +1136,15 @@ def run_vllm_e2e(args):
             res = json.loads(line[-1][len("VLLM_ARM_RESULT "):])
             res["process_seconds"] = round(time.time() - t0, 1)
             runs[arm].append(res)
+            meta.setdefault(arm, []).append(
+                {k: v for k, v in res.items() if k.endswith(("_calls", "_matches", "_names",
+                                                             "_seconds", "_layers"))})
     out = {"vllm_e2e": f"Llama-3.1-8B architecture W4A4 in vLLM, one B200, {input_len} in / "
                        f"{output_len} out, CUDA graphs, fusion passes off",
            "workload": args.vllm_workload, "repeats": args.vllm_repeats,
            "order": "arms interleaved, order rotated each repeat; one engine process per run",
-           "arms": {a: VLLM_ARMS[a] for a in arms}, "batch": {}, "failures": failures}
+           "arms": {a: VLLM_ARMS[a] for a in arms}, "batch": {}, "failures": failures,
+           "per_run": meta}
     for bs in batches:
         row = {}
         for arm in arms:

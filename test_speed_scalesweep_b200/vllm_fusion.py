@@ -77,6 +77,26 @@ def _example(*shape, dtype=torch.bfloat16):
     return torch.empty(*shape, dtype=dtype, device="cuda")
 
 
+def _norm_eps_is(eps):
+    """Inductor's pattern matcher treats float literals as wildcards, so a
+    pattern traced with one epsilon also matches norms with another.  Each
+    epsilon's pattern therefore accepts only a matched norm node that
+    carries its own epsilon, and the replacement passes that value on."""
+    targets = {"vllm_ir.rms_norm.default", "vllm_ir.fused_add_rms_norm.default"}
+
+    def check(match) -> bool:
+        for node in match.nodes:
+            if str(node.target) in targets:
+                floats = [a for a in node.args if isinstance(a, float)]
+                return bool(floats) and floats[-1] == eps
+        return False
+    return check
+
+
+def _all(*checks):
+    return lambda match: all(c(match) for c in checks)
+
+
 def _counted(kind, check):
     def extra_check(match) -> bool:
         ok = check(match)
@@ -133,11 +153,13 @@ def register_patterns(pm_pass) -> None:
                                 [_example(5, 32), _example(32), _example(5, 32),
                                  _example(1, dtype=torch.float32)],
                                 pm.fwd_only, pm_pass,
-                                extra_check=_counted("fused_add_rms_norm", _norm_supported))
+                                extra_check=_counted("fused_add_rms_norm",
+                                                     _all(_norm_eps_is(eps), _norm_supported)))
         pm.register_replacement(norm_p, norm_r,
                                 [_example(5, 32), _example(32), _example(1, dtype=torch.float32)],
                                 pm.fwd_only, pm_pass,
-                                extra_check=_counted("rms_norm", _norm_supported))
+                                extra_check=_counted("rms_norm",
+                                                     _all(_norm_eps_is(eps), _norm_supported)))
 
     def silu_replacement(input, scale):
         q = ops.silu_and_mul_scalesweep_mse_nvfp4_quant.default(input, scale, True)
@@ -191,7 +213,8 @@ def make_pass_class():
             self.matched_count = self.patterns.apply(graph)
 
         def uuid(self) -> str:
-            return self.hash_source(self, register_patterns, _norm_supported, _silu_supported)
+            return self.hash_source(self, register_patterns, _norm_supported, _silu_supported,
+                                    _norm_eps_is)
 
     return ScaleSweepQuantFusionPass
 

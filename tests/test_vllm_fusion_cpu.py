@@ -12,6 +12,19 @@ from test_speed_scalesweep_b200 import ops as _ops  # noqa: E402,F401
 from test_speed_scalesweep_b200 import vllm_fusion  # noqa: E402
 
 
+def _fused_eps(gm):
+    """The epsilon each fused norm op received, by op name."""
+    out = {}
+    for n in gm.graph.nodes:
+        if n.op != "call_function":
+            continue
+        if "rms_norm_scalesweep_mse_nvfp4_quant" in str(n.target):
+            out["rms_norm"] = n.args[2]
+        if "auto_functionalized" in str(n.target) and "fused_add_rms_norm_nvfp4" in str(n.args[0]):
+            out["fused_add_rms_norm"] = n.kwargs["epsilon"]
+    return out
+
+
 def _trace_and_fuse(fn, inputs):
     import torch._inductor.pattern_matcher as pm
     from torch._inductor.pattern_matcher import PatternMatcherPass
@@ -25,6 +38,7 @@ def _trace_and_fuse(fn, inputs):
             vllm_fusion.MATCHES[k] = 0
         count = pm_pass.apply(gm.graph)
     gm.graph.lint()
+    _trace_and_fuse.last_eps = _fused_eps(gm)
     # an auto_functionalized node names the in-place op it wraps as its first argument
     targets = [str(n.args[0]) if "auto_functionalized" in str(n.target) else str(n.target)
                for n in gm.graph.nodes if n.op == "call_function"]
@@ -57,6 +71,8 @@ def test_pass_fuses_norms_and_silu_into_the_quantizer():
     assert "scalesweep_b200.fused_add_rms_norm_nvfp4_quant" in joined
     assert "scalesweep_b200.silu_and_mul_scalesweep_mse_nvfp4_quant" in joined
     assert "vllm_ir.rms_norm" not in joined and "vllm_ir.fused_add_rms_norm" not in joined
+    # each fused op carries its own norm's epsilon (1e-5 for the fused add, 1e-6 for the plain)
+    assert _trace_and_fuse.last_eps == {"fused_add_rms_norm": 1e-5, "rms_norm": 1e-6}
 
 
 def _norm_then_quant_and_reuse(x, w, gsi):
