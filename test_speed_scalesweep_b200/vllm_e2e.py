@@ -169,8 +169,11 @@ LINEAR_CALLS = {"ours": 0, "fallback": 0}
 # its programmatic dependent launch, for the whole linear layer) beats vLLM's
 # CUTLASS NVFP4 GEMM, per Llama-3.1-8B shape (K, N); measured on B200 with
 # ``python bench.py --gemm-crossover``.  Larger M, and shapes not listed, use
-# vLLM's GEMM.
-OURS_UP_TO_M = {}
+# vLLM's GEMM.  Measured (vLLM time / this package's, one CUDA graph of 20
+# launches): qkv 1.07-1.16 and o 1.02-1.34 up to M=64, 0.65-0.94 from 96 to
+# 256; gate_up 1.16-1.97 and down 1.07-1.96 up to M=128, 0.75-0.87 at 192
+# and 256.
+OURS_UP_TO_M = {(4096, 6144): 64, (4096, 4096): 64, (4096, 28672): 128, (14336, 4096): 128}
 GEMM_DISPATCH = {"on": False, "ours": 0, "vllm": 0}
 
 
