@@ -97,6 +97,9 @@ def parse_args():
                     help="only run the NVFP4 GEMM 4 times on one shape and exit (for ncu)")
     ap.add_argument("--profile-amax", default=None, metavar="MxK",
                     help="only run the fused amax + global-scale kernel 4 times and exit")
+    ap.add_argument("--profile-amax-noalloc", default=None, metavar="MxK",
+                    help="only run the allocation-free global-scale entry point 4 times and "
+                         "exit (for ncu)")
     ap.add_argument("--profile-act", default=None, metavar="MxN",
                     help="only run silu_and_mul and the fused SiLU-and-mul quantizer on a "
                          "[M, 2N] input 4 times each and exit (for ncu)")
@@ -1040,6 +1043,29 @@ def run_profile_amax(args):
     print(json.dumps({"profile_amax": [m, k]}))
 
 
+def run_profile_amax_noalloc(args):
+    """The allocation-free global-scale entry point (fixed device scratch) 4
+    times on one [M, K] bf16 input, through the C ABI; for ncu."""
+    import ctypes
+    import torch
+    from test_speed_scalesweep_b200 import _lib
+    lib = _lib.lib()
+    m, k = (int(v) for v in args.profile_amax_noalloc.lower().split("x"))
+    if m * k > lib.ssw_global_scale_inv_noalloc_max_numel():
+        raise SystemExit("above the allocation-free entry point's maximum size")
+    x = make_shard(m, k, 7, torch.device("cuda", 0))
+    out = torch.empty(1, dtype=torch.float32, device=x.device)
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(4):
+        st = lib.ssw_global_scale_inv_noalloc(ctypes.c_void_p(x.data_ptr()), 0, x.numel(),
+                                              FP8_MAX, ctypes.c_void_p(out.data_ptr()), None,
+                                              ctypes.c_void_p(stream))
+        if st != 0:
+            raise SystemExit(f"ssw_global_scale_inv_noalloc returned {st}")
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_amax_noalloc": [m, k]}))
+
+
 def run_profile_act(args):
     import torch
     from test_speed_scalesweep_b200 import act_quant
@@ -1180,6 +1206,9 @@ def main():
         return
     if args.profile_amax:
         run_profile_amax(args)
+        return
+    if args.profile_amax_noalloc:
+        run_profile_amax_noalloc(args)
         return
     if args.profile_act:
         run_profile_act(args)
