@@ -558,6 +558,12 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
         results["fusion_pass_matches"] = dict(vllm_fusion.MATCHES)
         results["fusion"] = ("RMSNorm / fused-add RMSNorm / SiLU-and-mul + scale-sweep quant "
                              "fused by a vLLM compile pass (this package)")
+    if fused_norm or fusion_pass:
+        results["numerics"] = (
+            "the fused RMSNorm equals vLLM's vllm_c rms_norm / fused_add_rms_norm kernels bit "
+            "for bit; under Inductor vLLM runs a generated native RMSNorm instead, so the "
+            "normalised values (and then codes) can differ from an unfused compiled run in the "
+            "last bits; in eager mode both generate the same tokens")
     if fused_norm:
         results["decoder_hook_calls"] = dict(DECODER_CALLS)
         results["fusion"] = ("RMSNorm + scale-sweep quant (qkv, gate_up) and SiLU-and-mul + "
