@@ -58,7 +58,9 @@ VLLM_ARMS = {
                         "implementation (:546-560), SCALESWEEP_TUNE=0 as in run_bench_tune.sh",
     "scalesweep_mse": "this package's scalesweep_mse quantizer",
     "scalesweep_mse_fused_norm_act": "this package's quantizer with RMSNorm and SiLU-and-mul fused "
-                                     "into it (Llama module hooks)",
+                                     "into it (Llama module hooks); the fused RMSNorm is vLLM's "
+                                     "vllm_c kernel bit for bit, so under Inductor its last bits "
+                                     "can differ from the unfused compiled run",
     "scalesweep_mse_fusion_pass": "the same fusions reached through a vLLM compile pass "
                                   "(vllm_fusion.py) instead of module hooks",
     "scalesweep_mse_dispatch": "this package's quantizer; each linear layer's GEMM from this "
