@@ -98,7 +98,6 @@ int quant_out(const char* name, int variant, int mode, const void* input, int in
   p.bpc_pad = (uint32_t)((bpc_out + 3) / 4 * 4);
   ssw::make_divider(p.bpc_out, &p.div_magic, &p.div_shift);
   p.swizzled = swizzled ? 1 : 0;
-  p.scale_word_stores = (bpc_out % 4 == 0) && aligned(output_scale, 4);
   p.silu_row_elems = silu_mul ? 2 * (uint64_t)n : 0;
   p.norm_weight = norm_weight;
   p.norm_rstd = norm_rstd;

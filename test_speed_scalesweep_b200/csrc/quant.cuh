@@ -23,7 +23,6 @@ struct QuantParams {
   uint32_t div_magic;         // row = (umulhi(b, div_magic) + b) >> div_shift == b / bpc_out
   uint32_t div_shift;
   int swizzled;
-  int scale_word_stores;      // bpc_out % 4 == 0 and output_scale 4-byte aligned
   uint64_t silu_row_elems;    // SiLU-and-mul input only: elements per input row (2 * n)
   const uint16_t* norm_weight;  // RMSNorm front end only: bf16 weight [n]
   const float* norm_rstd;       // RMSNorm front end only: 1/rms of each row [rows]
