@@ -1185,17 +1185,30 @@ int choose_splits(int64_t m, int64_t n, int64_t k, int device_sms) {
   // add their partials in distributed shared memory, so a split needs only 4
   // K blocks of work.  More splits (very long K) reduce through global
   // memory, whose round trip (~2 us to publish a partial) needs at least 8 K
-  // blocks per split.  Measured on B200 (128-wide tiles, 2 CTAs per SM):
-  // splitting pays for long K (>= 32 K blocks: M=128, K=14336 19.9 -> 12.1
-  // us) and for tiles of <= 32 rows from 16 K blocks in 4 or more splits
-  // (M=16, N=4096, K=4096: 7.8 -> 6.5 us); 2-3 splits of a 16-block K, or
-  // any split of a 128-row tile at K=4096, lost to the unsplit 64-wide tile.
+  // blocks per split.  Measured on B200 (128-wide tiles, CUDA-graph replay):
+  // - long K (>= 32 K blocks): M=128, K=14336 19.9 -> 12.1 us;
+  // - a short K only for a partial M tile, in 4 or more splits (M=64,
+  //   N=4096, K=4096: 7.7 -> 6.8 us; a full 128-row tile gains nothing);
+  // - the 128-wide split tiles run two CTAs per SM, so over several M tiles,
+  //   and for tiles of <= 32 rows at a short K, a wave holds 2 x SMs CTAs
+  //   (M=256, N=4096, K=14336: 16.8 -> 15.3 us in 4 splits instead of 2;
+  //   M=16, N=6144, K=4096: 7.5 -> 6.9 us in 4 instead of none);
+  // - over several M tiles, powers of two: clusters of 3 pack badly next to
+  //   the second CTA of an SM (M=384, N=4096, K=14336: 27.0 us in 3 splits,
+  //   20.8 in 2).
   const int64_t tiles = (n / 128) * ((m + kBM - 1) / kBM);
   const int64_t kblocks = k / 256;
-  if (tiles >= device_sms) return 1;
   const bool long_k = kblocks >= 32;
-  if (!long_k && !(m <= 32 && kblocks >= 16)) return 1;
-  int64_t s = device_sms / tiles;
+  const int64_t wave =
+      (m > kBM || (!long_k && m <= 32)) ? 2 * (int64_t)device_sms : (int64_t)device_sms;
+  if (tiles >= wave) return 1;
+  if (!long_k && !(m <= 96 && kblocks >= 16)) return 1;
+  int64_t s = wave / tiles;
+  if (m > kBM) {
+    int64_t p = 1;
+    while (p * 2 <= s) p *= 2;
+    s = p;
+  }
   if (s > kblocks / 4) s = kblocks / 4;
   if (s > kMaxClusterSplits) {
     s = s < kblocks / 8 ? s : kblocks / 8;
@@ -1213,14 +1226,20 @@ int choose_tile_n(int64_t m, int64_t n, int splits, int device_sms) {
   // loses to the one-CTA tile when every pair gets a single tile).  Else,
   // enough 128 x 256 tiles to occupy most SMs (from ~60% of them the wide
   // tile wins): one CTA per 128 x 256 tile.
-  if (splits <= 1 && m > kBM && n % 256 == 0) {
-    if ((n / 256) * ((m + 2 * kBM - 1) / (2 * kBM)) > device_sms / 2) return kTilePair;
-    if ((n / 256) * ((m + kBM - 1) / kBM) * 5 >= (int64_t)device_sms * 3) return 256;
+  // The wide tile also serves a single M tile, down to decode sizes, when
+  // its 128 x 256 tiles fill the SMs (N=28672, K=4096: M=128 14.1 -> 12.1
+  // us, M=16 11.4 -> 9.7 us).
+  const int64_t m_tiles = (m + kBM - 1) / kBM;
+  if (splits <= 1 && n % 256 == 0) {
+    if (m > kBM && (n / 256) * ((m + 2 * kBM - 1) / (2 * kBM)) > device_sms / 2) return kTilePair;
+    if ((n / 256) * m_tiles * 5 >= (int64_t)device_sms * 3) return 256;
   }
-  // A single M tile whose 128-wide N tiles do not fill the SMs streams its
-  // weights through twice as many 64-wide tiles (each CTA's TMA stream is
-  // latency-bound, so more CTAs move more bytes).  Split-K keeps 128.
-  if (splits > 1 || m > kBM || n % 64 != 0) return 128;
+  // 128-wide N tiles that do not fill the SMs stream the weights through
+  // twice as many 64-wide tiles, as long as those still fit one wave of one
+  // CTA per SM (each CTA's TMA stream is latency-bound, so more CTAs move
+  // more bytes; M=256, N=4096: 9.2 -> 8.0 us).  Split-K keeps 128.
+  if (splits > 1 || n % 64 != 0) return 128;
+  if (m > kBM) return (n / 64) * m_tiles <= device_sms ? 64 : 128;
   return (n / 128) < device_sms ? 64 : 128;
 }
 

@@ -92,7 +92,7 @@ NVFP4_QUANT_CONFIG = {
 # (vllm_fusion.install_fusion_pass), so they apply to any model's graph.
 # "..._dispatch": as without the suffix, but each GEMM (with its quantizer,
 # where the hook issues both) is this package's where it is faster than vLLM's
-# at the call's token count (OURS_UP_TO_M), vLLM's elsewhere.
+# at the call's token count (OURS_M_RANGES), vLLM's elsewhere.
 BACKENDS = ("scalesweep_mse", "scalesweep_mse_reference", "rtn", "cutlass",
             "scalesweep_mse_linear", "scalesweep_mse_fused_act",
             "scalesweep_mse_fused_norm_act", "scalesweep_mse_fusion_pass",
@@ -165,20 +165,28 @@ def install_act_quant_hook(backend: str, op=None) -> int:
 
 LINEAR_CALLS = {"ours": 0, "fallback": 0}
 
-# Largest token count M at which this package's GEMM (with the quantizer as
-# its programmatic dependent launch, for the whole linear layer) beats vLLM's
-# CUTLASS NVFP4 GEMM, per Llama-3.1-8B shape (K, N); measured on B200 with
-# ``python bench.py --gemm-crossover``.  Larger M, and shapes not listed, use
-# vLLM's GEMM.  Measured (vLLM time / this package's, one CUDA graph of 20
-# launches): qkv 1.07-1.16 and o 1.02-1.34 up to M=64, 0.65-0.94 from 96 to
-# 256; gate_up 1.16-1.97 and down 1.07-1.96 up to M=128, 0.75-0.87 at 192
-# and 256.
-OURS_UP_TO_M = {(4096, 6144): 64, (4096, 4096): 64, (4096, 28672): 128, (14336, 4096): 128}
+# Token-count ranges (inclusive) in which this package's GEMM (with the
+# quantizer as its programmatic dependent launch, for the whole linear layer)
+# beats scale-sweep quantization followed by vLLM's CUTLASS NVFP4 GEMM, per
+# Llama-3.1-8B shape (K, N); measured on B200 with
+# ``python bench.py --gemm-crossover`` (vLLM time / this package's, one CUDA
+# graph of 20 launches):
+#   qkv     (4096, 6144):  1.05-1.32 up to M=64, 0.67-0.99 above;
+#   o       (4096, 4096):  1.09-1.35 up to M=64, 0.91-0.96 from 96 to 512;
+#   gate_up (4096, 28672): 1.19-2.05 up to M=128, 0.85-0.88 at 192-256,
+#                          1.06 at 384-512, 0.87-1.01 from 1024;
+#   down    (14336, 4096): 1.02-1.69 up to M=128, 0.94-0.96 at 192-256,
+#                          1.11-1.15 at 384-1024, 0.99-1.02 from 2048.
+# Other shapes and token counts use vLLM's GEMM.
+OURS_M_RANGES = {(4096, 6144): ((1, 64),), (4096, 4096): ((1, 64),),
+                 (4096, 28672): ((1, 128), (384, 512)),
+                 (14336, 4096): ((1, 128), (384, 1024))}
 GEMM_DISPATCH = {"on": False, "ours": 0, "vllm": 0}
 
 
 def _ours_for(m: int, n: int, k: int) -> bool:
-    return m <= OURS_UP_TO_M.get((k, n), 0) and k % 256 == 0 and n % 128 == 0
+    return (k % 256 == 0 and n % 128 == 0 and
+            any(lo <= m <= hi for lo, hi in OURS_M_RANGES.get((k, n), ())))
 
 
 _DISPATCH_LIB = None
@@ -188,7 +196,7 @@ def register_dispatch_ops() -> None:
     """``scalesweep_b200::nvfp4_mm_dispatch`` and
     ``scalesweep_b200::scalesweep_nvfp4_linear_dispatch``: the GEMM, or the
     whole W4A4 linear layer, from this package where it is faster
-    (``OURS_UP_TO_M``) and from vLLM's CUTLASS kernel elsewhere.  The choice
+    (``OURS_M_RANGES``) and from vLLM's CUTLASS kernel elsewhere.  The choice
     is made at run time from the actual token count, inside an op that
     torch.compile treats as opaque, so one compiled graph serves every M.
     Idempotent."""
@@ -552,8 +560,8 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
     if dispatch:
         results["gemm_dispatch_calls"] = {"ours": GEMM_DISPATCH["ours"],
                                           "vllm": GEMM_DISPATCH["vllm"]}
-        results["linear_backend"] = ("this package's GEMM up to OURS_UP_TO_M tokens, "
-                                     "vLLM CUTLASS above")
+        results["linear_backend"] = ("this package's GEMM in the OURS_M_RANGES token counts, "
+                                     "vLLM CUTLASS elsewhere")
     if fusion_pass:
         results["fusion_pass_matches"] = dict(vllm_fusion.MATCHES)
         results["fusion"] = ("RMSNorm / fused-add RMSNorm / SiLU-and-mul + scale-sweep quant "

@@ -60,8 +60,15 @@ def test_gemm_matches_dequant_matmul_oracle(lib, m, n, k):
     assert err <= TOL, err
 
 
+# The tile choices between one and four M tiles: 64-wide tiles over two M
+# tiles (256 and 160 rows at N=4096), 128 x 256 tiles for one M tile of any
+# rows (full and trimmed A boxes at N=28672, down to 16 rows), 4 or 2
+# cluster splits over two and four M tiles at K=14336, and 4 splits of a
+# 1-row tile at N=6144.
 @pytest.mark.parametrize("m,n,k", [(16, 6144, 4096), (128, 4096, 4096), (1024, 4096, 14336),
-                                   (8192, 4096, 4096)])
+                                   (8192, 4096, 4096), (256, 4096, 4096), (160, 4096, 4096),
+                                   (128, 28672, 4096), (96, 28672, 4096), (256, 4096, 14336),
+                                   (512, 4096, 14336), (16, 28672, 4096), (1, 6144, 4096)])
 def test_gemm_matches_vllm_cutlass_fp4_gemm(lib, m, n, k):
     vops = pytest.importorskip("vllm._custom_ops")
     if not hasattr(torch.ops, "_C") or not hasattr(torch.ops._C, "cutlass_scaled_fp4_mm"):

@@ -119,11 +119,13 @@ def test_fused_norm_hook_feeds_each_norm_to_the_next_projections_quantizer(monke
 
 def test_gemm_dispatch_rule_and_shapes(monkeypatch):
     vllm_e2e.register_dispatch_ops()
-    monkeypatch.setattr(vllm_e2e, "OURS_UP_TO_M", {(4096, 28672): 64})
+    monkeypatch.setattr(vllm_e2e, "OURS_M_RANGES", {(4096, 28672): ((1, 64), (384, 512))})
     assert vllm_e2e._ours_for(64, 28672, 4096)
-    assert not vllm_e2e._ours_for(65, 28672, 4096)       # above the measured crossover
+    assert not vllm_e2e._ours_for(65, 28672, 4096)       # between the measured ranges
+    assert vllm_e2e._ours_for(384, 28672, 4096) and vllm_e2e._ours_for(512, 28672, 4096)
+    assert not vllm_e2e._ours_for(513, 28672, 4096)
     assert not vllm_e2e._ours_for(16, 6144, 4096)        # shape not listed: vLLM's GEMM
-    monkeypatch.setattr(vllm_e2e, "OURS_UP_TO_M", {(4000, 28672): 64})
+    monkeypatch.setattr(vllm_e2e, "OURS_M_RANGES", {(4000, 28672): ((1, 64),)})
     assert not vllm_e2e._ours_for(16, 28672, 4000)       # K the GEMM does not take
     meta = dict(device="meta")
     a = torch.empty(16, 2048, dtype=torch.uint8, **meta)
