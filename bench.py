@@ -1165,8 +1165,8 @@ def run_vllm_e2e(args):
             res["process_seconds"] = round(time.time() - t0, 1)
             runs[arm].append(res)
             meta.setdefault(arm, []).append(
-                {k: v for k, v in res.items() if k.endswith(("_calls", "_matches", "_names",
-                                                             "_seconds", "_layers"))})
+                {k: v for k, v in res.items()
+                 if "_calls" in k or k.endswith(("_matches", "_names", "_seconds", "_layers"))})
     out = {"vllm_e2e": f"Llama-3.1-8B architecture W4A4 in vLLM, one B200, {input_len} in / "
                        f"{output_len} out, CUDA graphs, fusion passes off",
            "workload": args.vllm_workload, "repeats": args.vllm_repeats,
