@@ -30,7 +30,9 @@ bf16 output.  vLLM's own fusion passes make the same substitution.
 ``install_fusion_pass()`` appends the pass to vLLM's ``PostGradPassManager``,
 after vLLM's own passes and before IR lowering.  It then applies to any model
 whose compiled graph holds these producer -> quantizer pairs, not only to
-Llama's modules.  ``MATCHES`` counts the rewrites per pattern kind.
+Llama's modules.  ``MATCHES`` counts, per pattern kind, the matches its
+check accepted (Inductor compiles each distinct graph piece once, so
+identical decoder layers count once).
 """
 from __future__ import annotations
 
