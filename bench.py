@@ -68,6 +68,8 @@ VLLM_ARMS = {
                                "is faster, vLLM's CUTLASS GEMM elsewhere",
     "scalesweep_mse_fused_norm_act_dispatch": "the fused RMSNorm/SiLU-and-mul hooks with the "
                                               "same per-call GEMM choice",
+    "scalesweep_mse_fusion_pass_dispatch": "the compile-pass fusions (any model) with the GEMM "
+                                           "alone dispatched per call",
 }
 # (input tokens, output tokens, batch sizes): config 4, and the reference's
 # own 256-request run (benchmark_nvfp4_tokens.py defaults, run_bench_tune.sh)

@@ -92,11 +92,14 @@ NVFP4_QUANT_CONFIG = {
 # (vllm_fusion.install_fusion_pass), so they apply to any model's graph.
 # "..._dispatch": as without the suffix, but each GEMM (with its quantizer,
 # where the hook issues both) is this package's where it is faster than vLLM's
-# at the call's token count (OURS_M_RANGES), vLLM's elsewhere.
+# at the call's token count (OURS_M_RANGES), vLLM's elsewhere.  With the
+# compile pass, only the GEMM is dispatched (install_gemm_hook), so the
+# quantizer stays visible to the pass.
 BACKENDS = ("scalesweep_mse", "scalesweep_mse_reference", "rtn", "cutlass",
             "scalesweep_mse_linear", "scalesweep_mse_fused_act",
             "scalesweep_mse_fused_norm_act", "scalesweep_mse_fusion_pass",
-            "scalesweep_mse_dispatch", "scalesweep_mse_fused_norm_act_dispatch")
+            "scalesweep_mse_dispatch", "scalesweep_mse_fused_norm_act_dispatch",
+            "scalesweep_mse_fusion_pass_dispatch")
 _OP_FOR_BACKEND = {"scalesweep_mse": "scalesweep_mse_nvfp4_quant",
                    "scalesweep_mse_reference": "scalesweep_mse_reference_nvfp4_quant",
                    "rtn": "rtn_nvfp4_quant"}
@@ -163,6 +166,52 @@ def install_act_quant_hook(backend: str, op=None) -> int:
     return rebound
 
 
+GEMM_HOOK_CALLS = {"count": 0}
+
+
+def install_gemm_hook() -> int:
+    """Route the GEMM of vLLM's W4A4 linear layer through
+    ``scalesweep_b200::nvfp4_mm_dispatch`` (this package's GEMM where it is
+    faster at the call's token count, vLLM's elsewhere) and leave the rest of
+    ``CutlassNvFp4LinearKernel.apply_weights`` as it is.
+
+    ``apply_weights`` calls the module-local name ``cutlass_scaled_fp4_mm``
+    (vllm 0.22 ``model_executor/kernels/linear/nvfp4/cutlass.py:64-71``); this
+    rebinds it, the pattern the reference applies to the same name in
+    ``benchmark_nvfp4_tokens.py:195``.  The activation quantizer stays a
+    separate op in the graph, so ``vllm_fusion``'s pass can still fuse its
+    producer into it.  bf16 outputs only; others keep vLLM's GEMM.  Returns
+    the number of module-level names rebound."""
+    import importlib
+    import sys
+
+    import vllm._custom_ops as vllm_ops
+
+    register_dispatch_ops()
+    for mod_name in ("vllm.model_executor.kernels.linear.nvfp4.cutlass",):
+        try:
+            importlib.import_module(mod_name)
+        except Exception:  # pragma: no cover - depends on the vLLM build
+            pass
+    original = vllm_ops.cutlass_scaled_fp4_mm
+
+    def cutlass_scaled_fp4_mm(a, b, block_scale_a, block_scale_b, alpha, out_dtype):
+        GEMM_HOOK_CALLS["count"] += 1
+        if out_dtype != torch.bfloat16:
+            return original(a, b, block_scale_a, block_scale_b, alpha, out_dtype)
+        return torch.ops.scalesweep_b200.nvfp4_mm_dispatch(a, b, block_scale_a, block_scale_b,
+                                                           alpha)
+
+    # the callers' module-local names only: vllm._custom_ops keeps its own
+    rebound = 0
+    for name, mod in list(sys.modules.items()):
+        if (name.startswith("vllm") and name != "vllm._custom_ops"
+                and getattr(mod, "cutlass_scaled_fp4_mm", None) is original):
+            setattr(mod, "cutlass_scaled_fp4_mm", cutlass_scaled_fp4_mm)
+            rebound += 1
+    return rebound
+
+
 LINEAR_CALLS = {"ours": 0, "fallback": 0}
 
 # Token-count ranges (inclusive) in which this package's GEMM (with the
@@ -185,7 +234,7 @@ GEMM_DISPATCH = {"on": False, "ours": 0, "vllm": 0}
 
 
 def _ours_for(m: int, n: int, k: int) -> bool:
-    return (k % 256 == 0 and n % 128 == 0 and
+    return (k % 256 == 0 and n % 64 == 0 and
             any(lo <= m <= hi for lo, hi in OURS_M_RANGES.get((k, n), ())))
 
 
@@ -209,6 +258,9 @@ def register_dispatch_ops() -> None:
     from .gemm import cutlass_scaled_fp4_mm, scalesweep_nvfp4_linear
     from .scalesweep_mse_nvfp4_utils import scalesweep_mse_nvfp4_quant_impl
 
+    # vLLM's own GEMM, bound now: the GEMM hook may later rebind the name
+    # in vLLM's modules to a function that calls back into this op
+    vllm_mm = vllm_ops.cutlass_scaled_fp4_mm
     lib = torch.library.Library("scalesweep_b200", "FRAGMENT")
     lib.define("nvfp4_mm_dispatch(Tensor a, Tensor b, Tensor a_scale, Tensor b_scale, "
                "Tensor alpha) -> Tensor")
@@ -221,7 +273,7 @@ def register_dispatch_ops() -> None:
             GEMM_DISPATCH["ours"] += 1
             return cutlass_scaled_fp4_mm(a, b, a_scale, b_scale, alpha)
         GEMM_DISPATCH["vllm"] += 1
-        return vllm_ops.cutlass_scaled_fp4_mm(a, b, a_scale, b_scale, alpha, torch.bfloat16)
+        return vllm_mm(a, b, a_scale, b_scale, alpha, torch.bfloat16)
 
     def linear(x, input_scale, weight, weight_scale, alpha):
         m, k, n = x.shape[0], x.shape[1], weight.shape[0]
@@ -230,8 +282,7 @@ def register_dispatch_ops() -> None:
             return scalesweep_nvfp4_linear(x, input_scale, weight, weight_scale, alpha)
         GEMM_DISPATCH["vllm"] += 1
         codes, scales = scalesweep_mse_nvfp4_quant_impl(x, input_scale, True)
-        return vllm_ops.cutlass_scaled_fp4_mm(codes, weight, scales, weight_scale, alpha,
-                                              x.dtype)
+        return vllm_mm(codes, weight, scales, weight_scale, alpha, x.dtype)
 
     def fake_mm(a, b, a_scale, b_scale, alpha):
         return a.new_empty((a.shape[0], b.shape[0]), dtype=torch.bfloat16)
@@ -258,7 +309,7 @@ def install_linear_hook(dispatch: bool = False) -> None:
     makes one call of the registered op
     ``torch.ops.scalesweep_b200.scalesweep_nvfp4_linear``: this package's
     quantizer, then its GEMM as a programmatic dependent launch.  Layers the
-    GEMM does not take (K-padded weights, K % 256, N % 128, non-bf16
+    GEMM does not take (K-padded weights, K % 256, N % 64, non-bf16
     activations) keep vLLM's method.
     """
     from . import ops  # noqa: F401  (registers torch.ops.scalesweep_b200.*)
@@ -275,7 +326,7 @@ def install_linear_hook(dispatch: bool = False) -> None:
     def apply_weights(self, layer, x, bias=None):
         k = x.shape[-1]
         n = layer.weight.shape[0]
-        if (getattr(layer, "weights_padding_cols", 0) or k % 256 or n % 128
+        if (getattr(layer, "weights_padding_cols", 0) or k % 256 or n % 64
                 or x.dtype != torch.bfloat16):
             LINEAR_CALLS["fallback"] += 1
             return original(self, layer, x, bias)
@@ -495,7 +546,11 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
     if dispatch:
         register_dispatch_ops()
         GEMM_DISPATCH["on"] = True
-        install_linear_hook(dispatch=True)
+        if fusion_pass:
+            # keep the quantizer visible to the pass; dispatch the GEMM alone
+            install_gemm_hook()
+        else:
+            install_linear_hook(dispatch=True)
     if fusion_pass:
         from . import vllm_fusion
         vllm_fusion.install_fusion_pass()
@@ -560,6 +615,8 @@ def run(backend: str, batch_sizes, input_len: int, output_len: int, seed: int = 
     if dispatch:
         results["gemm_dispatch_calls"] = {"ours": GEMM_DISPATCH["ours"],
                                           "vllm": GEMM_DISPATCH["vllm"]}
+        if fusion_pass:
+            results["gemm_hook_calls"] = dict(GEMM_HOOK_CALLS)
         results["linear_backend"] = ("this package's GEMM in the OURS_M_RANGES token counts, "
                                      "vLLM CUTLASS elsewhere")
     if fusion_pass:

@@ -38,8 +38,9 @@ def test_linear_hook_routes_supported_layers_and_falls_back(monkeypatch):
     padded = _layer(padding=8)
     assert apply(None, padded, x) == "vllm" and seen == [padded]
     assert apply(None, _layer(), x.float()) == "vllm"            # not bf16
-    assert apply(None, _layer(n=6144 + 64), x) == "vllm"         # N % 128
-    assert vllm_e2e.LINEAR_CALLS == {"ours": 1, "fallback": 3}
+    assert apply(None, _layer(n=6144 + 32), x) == "vllm"         # N % 64
+    assert apply(None, _layer(n=6144 + 64), x).shape == (2, 5, 6144 + 64)  # 64-wide tiles
+    assert vllm_e2e.LINEAR_CALLS == {"ours": 2, "fallback": 3}
 
 
 def test_fused_act_hook_feeds_gate_up_to_the_fused_quantizer(monkeypatch):
@@ -148,3 +149,30 @@ def test_linear_hook_with_dispatch_calls_the_dispatch_op(monkeypatch):
     x = torch.empty(3, 4096, dtype=torch.bfloat16, device="meta")
     out = apply(None, _layer(n=4096), x)
     assert out.shape == (3, 4096)
+
+
+def test_gemm_hook_rebinds_the_module_local_name(monkeypatch):
+    import vllm._custom_ops as vllm_ops
+    seen = []
+
+    def original(a, b, sa, sb, alpha, out_dtype):
+        seen.append(out_dtype)
+        return "vllm"
+
+    monkeypatch.setattr(vllm_ops, "cutlass_scaled_fp4_mm", original)
+    monkeypatch.setattr(vllm_cutlass, "cutlass_scaled_fp4_mm", original)
+    assert vllm_e2e.install_gemm_hook() >= 1
+    hooked = vllm_cutlass.cutlass_scaled_fp4_mm
+    assert hooked is not original
+    # vLLM's own module keeps its GEMM, which the dispatch op calls for the
+    # token counts it leaves to vLLM (rebinding it would recurse)
+    assert vllm_ops.cutlass_scaled_fp4_mm is original
+    meta = dict(device="meta")
+    a = torch.empty(16, 2048, dtype=torch.uint8, **meta)
+    b = torch.empty(4096, 2048, dtype=torch.uint8, **meta)
+    sa = torch.empty(128, 256, dtype=torch.float8_e4m3fn, **meta)
+    sb = torch.empty(4096, 256, dtype=torch.float8_e4m3fn, **meta)
+    alpha = torch.empty(1, **meta)
+    out = hooked(a, b, sa, sb, alpha, torch.bfloat16)     # through the dispatch op
+    assert out.shape == (16, 4096) and out.dtype == torch.bfloat16
+    assert hooked(a, b, sa, sb, alpha, torch.float16) == "vllm" and seen == [torch.float16]
