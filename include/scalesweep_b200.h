@@ -200,7 +200,7 @@ int ssw_global_scale_inv(const void* input, int input_dtype, int64_t numel, floa
  * a: [m, k/2] E2M1 codes, b: [n, k/2] E2M1 codes (both K-major, element 2j in
  * the low nibble), a_scale / b_scale: E4M3 scales in the CUTLASS 128x4
  * swizzled layout (as written by the quantizers above, is_sf_swizzled_layout=1),
- * out: [m, n] bf16 row-major.  Requires k % 256 == 0 and n % 128 == 0
+ * out: [m, n] bf16 row-major.  Requires k % 256 == 0 and n % 64 == 0
  * (SSW_ERR_UNSUPPORTED otherwise) and 16-byte aligned pointers.
  * When the output has too few 128x128 tiles to fill the GPU and K is long
  * enough, the K loop is split across CTAs.  Splitting is opted into with a

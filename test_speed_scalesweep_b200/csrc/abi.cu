@@ -157,8 +157,8 @@ int gemm_shape_check(const char* name, int64_t m, int64_t n, int64_t k) {
   if (k % 256)
     return fail(SSW_ERR_UNSUPPORTED, "%s: k must be a multiple of 256 (got %lld)", name,
                 (long long)k);
-  if (n % 128)
-    return fail(SSW_ERR_UNSUPPORTED, "%s: n must be a multiple of 128 (got %lld)", name,
+  if (n % 64)
+    return fail(SSW_ERR_UNSUPPORTED, "%s: n must be a multiple of 64 (got %lld)", name,
                 (long long)n);
   if (m >= (1ll << 31) || n >= (1ll << 31) || k >= (1ll << 31))
     return fail(SSW_ERR_INVALID_ARGUMENT, "%s: sizes must be below 2^31", name);
@@ -373,7 +373,7 @@ int ssw_rtn_nvfp4_quant_out(const void* input, int input_dtype, int64_t num_rows
 
 int64_t ssw_nvfp4_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   int sms = 0;
-  if (m <= 0 || n <= 0 || k <= 0 || n % 128 || k % 256 || device_sms(&sms) != SSW_OK) return 0;
+  if (m <= 0 || n <= 0 || k <= 0 || n % 64 || k % 256 || device_sms(&sms) != SSW_OK) return 0;
   return (int64_t)ssw::gemm::workspace_bytes(m, n, k, ssw::gemm::choose_splits(m, n, k, sms));
 }
 
@@ -388,7 +388,7 @@ int ssw_nvfp4_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
 
 int64_t ssw_nvfp4_quant_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   int sms = 0;
-  if (m <= 0 || n <= 0 || k <= 0 || n % 128 || k % 256 || device_sms(&sms) != SSW_OK) return 0;
+  if (m <= 0 || n <= 0 || k <= 0 || n % 64 || k % 256 || device_sms(&sms) != SSW_OK) return 0;
   return (int64_t)quant_gemm_layout(m, n, k, sms).total;
 }
 

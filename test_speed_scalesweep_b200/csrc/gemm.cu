@@ -1196,6 +1196,8 @@ int choose_splits(int64_t m, int64_t n, int64_t k, int device_sms) {
   // - over several M tiles, powers of two: clusters of 3 pack badly next to
   //   the second CTA of an SM (M=384, N=4096, K=14336: 27.0 us in 3 splits,
   //   20.8 in 2).
+  // N % 128 == 64 runs the unsplit 64-wide tile only
+  if (n % 128) return 1;
   const int64_t tiles = (n / 128) * ((m + kBM - 1) / kBM);
   const int64_t kblocks = k / 256;
   const bool long_k = kblocks >= 32;
@@ -1226,6 +1228,9 @@ int choose_tile_n(int64_t m, int64_t n, int splits, int device_sms) {
   // loses to the one-CTA tile when every pair gets a single tile).  Else,
   // enough 128 x 256 tiles to occupy most SMs (from ~60% of them the wide
   // tile wins): one CTA per 128 x 256 tile.
+  // N % 128 == 64: 64-wide tiles; the last one is the first half of a
+  // 128-row scale slab (swizzled scale buffers hold whole slabs).
+  if (n % 128) return 64;
   // The wide tile also serves a single M tile, down to decode sizes, when
   // its 128 x 256 tiles fill the SMs (N=28672, K=4096: M=128 14.1 -> 12.1
   // us, M=16 11.4 -> 9.7 us).

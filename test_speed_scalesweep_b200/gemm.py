@@ -20,7 +20,7 @@ def cutlass_scaled_fp4_mm(a: torch.Tensor, b: torch.Tensor, block_scale_a: torch
 
     a: uint8 [M, K/2] E2M1 codes; b: uint8 [N, K/2]; block_scale_a/b: E4M3
     scales in the 128x4-swizzled layout; alpha: float32 device scalar.
-    K must be a multiple of 256 and N a multiple of 128.  When the output has
+    K must be a multiple of 256 and N a multiple of 64.  When the output has
     too few tiles to fill the GPU the K loop is split across CTAs (workspace
     from torch's caching allocator); ``split_k=False`` forces one pass.
     """

@@ -27,7 +27,7 @@ def _quant_gemm(h, m=16, n=128, k=256, x=0x1000, dtype=0):
 
 @pytest.mark.parametrize("kwargs,status,needle", [
     (dict(k=300), _lib.SSW_ERR_UNSUPPORTED, "multiple of 256"),
-    (dict(n=100), _lib.SSW_ERR_UNSUPPORTED, "multiple of 128"),
+    (dict(n=100), _lib.SSW_ERR_UNSUPPORTED, "multiple of 64"),
     (dict(m=-1), _lib.SSW_ERR_INVALID_ARGUMENT, "bad sizes"),
     (dict(m=1 << 31), _lib.SSW_ERR_INVALID_ARGUMENT, "below 2^31"),
     (dict(a=0), _lib.SSW_ERR_INVALID_ARGUMENT, "null"),
@@ -41,7 +41,7 @@ def test_gemm_rejects_bad_arguments_without_a_gpu(built_library, kwargs, status,
 
 @pytest.mark.parametrize("kwargs,status,needle", [
     (dict(k=300), _lib.SSW_ERR_UNSUPPORTED, "multiple of 256"),
-    (dict(n=100), _lib.SSW_ERR_UNSUPPORTED, "multiple of 128"),
+    (dict(n=100), _lib.SSW_ERR_UNSUPPORTED, "multiple of 64"),
     (dict(m=-1), _lib.SSW_ERR_INVALID_ARGUMENT, "bad sizes"),
 ])
 def test_quant_gemm_rejects_bad_shapes_without_a_gpu(built_library, kwargs, status, needle):

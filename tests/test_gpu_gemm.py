@@ -41,10 +41,13 @@ def _rel_fro(got, ref):
 # and two tiles for some pairs, so the ring wraps across tiles.
 # One-CTA 128x256 tiles: (1281, 2560, 512), (1458, 2560, 2048).
 # (64, 4096, 1024): 128x64 tiles, upper-half scale columns.
+# (16, 192, 512), (200, 320, 1024): N % 128 == 64, the last 64-wide tile in
+# the first half of a padded scale slab (one and two M tiles).
 @pytest.mark.parametrize("m,n,k", [(128, 128, 256), (16, 256, 512), (200, 384, 1024),
                                    (1, 128, 4096), (1024, 512, 4096), (2000, 2560, 512),
                                    (1793, 2560, 512), (1970, 2560, 2048), (1400, 4608, 768),
-                                   (1281, 2560, 512), (1458, 2560, 2048), (64, 4096, 1024)])
+                                   (1281, 2560, 512), (1458, 2560, 2048), (64, 4096, 1024),
+                                   (16, 192, 512), (200, 320, 1024)])
 def test_gemm_matches_dequant_matmul_oracle(lib, m, n, k):
     from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm
     _, gsi_a, qa, sa = _quantized(m, k, 1 + m, 1.0, "scalesweep_mse")
