@@ -222,6 +222,22 @@ int ssw_nvfp4_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
                    int64_t k, void* workspace, int64_t workspace_bytes, int* status,
                    void* stream);
 
+/* ssw_nvfp4_gemm launched as a programmatic dependent of the kernel before it
+ * on the stream (typically the quantizer that wrote a and a_scale).  Its
+ * prologue and the loads of b and b_scale may overlap that kernel; a and
+ * a_scale are read only after it has finished and its writes are visible.
+ * Correct after any kernel (one that does not signal early is simply waited
+ * for); the split-K path through global memory launches without the
+ * dependency.  Same arguments, results and errors as ssw_nvfp4_gemm.
+ * Replaces the same vLLM call as ssw_nvfp4_gemm (cutlass_scaled_fp4_mm right
+ * after scaled_fp4_quant, vllm/model_executor/kernels/linear/nvfp4/
+ * cutlass.py:56-71).
+ */
+int ssw_nvfp4_gemm_dependent(const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
+                             const uint8_t* b_scale, const float* alpha, void* out, int64_t m,
+                             int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
+                             int* status, void* stream);
+
 /*
  * A W4A4 linear layer's activation quantization and GEMM in one call:
  * x [m, k] (bf16/f16) is quantized with the "scalesweep_mse" sweep

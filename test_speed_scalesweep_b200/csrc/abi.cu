@@ -386,6 +386,15 @@ int ssw_nvfp4_gemm(const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
                      workspace_bytes, status, stream, false);
 }
 
+int ssw_nvfp4_gemm_dependent(const uint8_t* a, const uint8_t* b, const uint8_t* a_scale,
+                             const uint8_t* b_scale, const float* alpha, void* out, int64_t m,
+                             int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
+                             int* status, void* stream) {
+  g_last_error.clear();
+  return gemm_common("nvfp4_gemm_dependent", a, b, a_scale, b_scale, alpha, out, m, n, k,
+                     workspace, workspace_bytes, status, stream, true);
+}
+
 int64_t ssw_nvfp4_quant_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   int sms = 0;
   if (m <= 0 || n <= 0 || k <= 0 || n % 64 || k % 256 || device_sms(&sms) != SSW_OK) return 0;

@@ -15,7 +15,8 @@ def cutlass_scaled_fp4_mm(a: torch.Tensor, b: torch.Tensor, block_scale_a: torch
                           block_scale_b: torch.Tensor, alpha: torch.Tensor,
                           out_dtype: torch.dtype = torch.bfloat16,
                           status: torch.Tensor | None = None,
-                          split_k: bool = True) -> torch.Tensor:
+                          split_k: bool = True,
+                          dependent_launch: bool = False) -> torch.Tensor:
     """``alpha * (A ⊙ sfA) @ (B ⊙ sfB)^T`` in bf16.
 
     a: uint8 [M, K/2] E2M1 codes; b: uint8 [N, K/2]; block_scale_a/b: E4M3
@@ -23,6 +24,9 @@ def cutlass_scaled_fp4_mm(a: torch.Tensor, b: torch.Tensor, block_scale_a: torch
     K must be a multiple of 256 and N a multiple of 64.  When the output has
     too few tiles to fill the GPU the K loop is split across CTAs (workspace
     from torch's caching allocator); ``split_k=False`` forces one pass.
+    ``dependent_launch=True`` launches it as a programmatic dependent of the
+    kernel before it on the stream (``ssw_nvfp4_gemm_dependent``): its
+    prologue and weight loads overlap that kernel, and A is read only after it.
     """
     if out_dtype != torch.bfloat16:
         raise ValueError("only bf16 output is implemented")
@@ -52,7 +56,8 @@ def cutlass_scaled_fp4_mm(a: torch.Tensor, b: torch.Tensor, block_scale_a: torch
     with torch.cuda.device(a.device):
         ws_bytes = int(h.ssw_nvfp4_gemm_workspace_bytes(m, n, k)) if split_k else 0
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=a.device) if ws_bytes else None
-        st = h.ssw_nvfp4_gemm(
+        fn = h.ssw_nvfp4_gemm_dependent if dependent_launch else h.ssw_nvfp4_gemm
+        st = fn(
             ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()),
             ctypes.c_void_p(block_scale_a.data_ptr()), ctypes.c_void_p(block_scale_b.data_ptr()),
             ctypes.c_void_p(alpha.data_ptr()), ctypes.c_void_p(out.data_ptr()), m, n, k,

@@ -271,7 +271,9 @@ def register_dispatch_ops() -> None:
         m, n, k = a.shape[0], b.shape[0], a.shape[1] * 2
         if _ours_for(m, n, k):
             GEMM_DISPATCH["ours"] += 1
-            return cutlass_scaled_fp4_mm(a, b, a_scale, b_scale, alpha)
+            # the codes come from the quantizer launched just before: start
+            # the prologue and weight loads while it finishes
+            return cutlass_scaled_fp4_mm(a, b, a_scale, b_scale, alpha, dependent_launch=True)
         GEMM_DISPATCH["vllm"] += 1
         return vllm_mm(a, b, a_scale, b_scale, alpha, torch.bfloat16)
 

@@ -133,3 +133,27 @@ def test_quant_gemm_linear_equals_quantize_then_gemm(lib, m, n, k):
     assert torch.equal(via_op, ref)
     for g in again:
         assert torch.equal(g, ref)
+
+
+# The GEMM as a programmatic dependent of the kernel before it on the stream:
+# right after the quantizer that writes A (unsplit 64-wide and wide tiles,
+# cluster split-K), and after a kernel that does not signal early (a torch
+# copy); the global-memory split launches without the dependency.
+@pytest.mark.parametrize("m,n,k", [(16, 6144, 4096), (16, 28672, 4096), (16, 4096, 14336),
+                                   (1, 128, 8192), (256, 4096, 4096), (16, 1024, 20480)])
+def test_dependent_gemm_equals_plain_gemm(lib, m, n, k):
+    from test_speed_scalesweep_b200 import custom
+    from test_speed_scalesweep_b200.gemm import cutlass_scaled_fp4_mm
+    x, gsi_a, qa, sa = _quantized(m, k, 51 + m, 1.0, "scalesweep_mse")
+    _, gsi_b, qb, sb = _quantized(n, k, 52 + n, 0.02, "rtn")
+    alpha = (1.0 / (gsi_a * gsi_b)).reshape(1).float()
+    ref = cutlass_scaled_fp4_mm(qa, qb, sa, sb, alpha)
+    outs = []
+    for _ in range(3):
+        ca, csa = custom.nvfp4_quant(x, gsi_a, True, "scalesweep_mse")
+        outs.append(cutlass_scaled_fp4_mm(ca, qb, csa, sb, alpha, dependent_launch=True))
+    a_copy = qa.clone()
+    outs.append(cutlass_scaled_fp4_mm(a_copy, qb, sa, sb, alpha, dependent_launch=True))
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o, ref)
