@@ -566,6 +566,45 @@ def run_norm_fusion_sweep(device, reps: int = 20):
     return out
 
 
+def measure_fp4_peak(device, iters: int = 4096):
+    """Dense FP4 tensor-core rate of this B200, measured: one CTA per SM
+    issues back-to-back kind::mxf4nvf4 MMAs (ssw_nvfp4_mma_rate_probe, the
+    GEMM's own instruction and layouts, no loads).  Returns TFLOP/s over the
+    whole GPU from CUDA events (best of 3 launches) and FLOPs per SM cycle."""
+    import ctypes
+    import torch
+    from test_speed_scalesweep_b200 import _lib
+    lib = _lib.lib()
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    cycles = torch.zeros(sms, dtype=torch.int64, device=device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device)
+    best = {}
+    for bn in (128, 256):
+        flops = 2.0 * 128 * bn * 64 * 4 * iters * sms
+        times = []
+        for _ in range(4):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            st = lib.ssw_nvfp4_mma_rate_probe(bn, iters, ctypes.c_void_p(cycles.data_ptr()),
+                                              ctypes.c_void_p(status.data_ptr()),
+                                              ctypes.c_void_p(stream.cuda_stream))
+            b.record(stream)
+            _lib.check(st)
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        if status.item() != 0 or int(cycles.min().item()) <= 0:
+            raise RuntimeError("tensor-core rate probe: a bounded wait gave up")
+        per_cycle = 2.0 * 128 * bn * 64 * 4 * iters / float(cycles.median().item())
+        best[bn] = {"tflops": round(flops / (min(times[1:]) * 1e-3) / 1e12, 1),
+                    "flops_per_sm_cycle": round(per_cycle, 1)}
+    top = max(best.values(), key=lambda v: v["tflops"])
+    return {"peak_tflops": top["tflops"], "by_tile_n": best,
+            "method": f"ssw_nvfp4_mma_rate_probe: {sms} CTAs, 4 x {iters} back-to-back "
+                      "kind::mxf4nvf4 MMAs (128 x N x 64) each, CUDA events, best of 3"}
+
+
 def run_gemm_sweep(device, reps: int = 20):
     """Config 3: quantize + tcgen05 NVFP4 GEMM on the Llama-3.1-8B linear shapes.
 
@@ -582,8 +621,14 @@ def run_gemm_sweep(device, reps: int = 20):
             else None
     except Exception:
         vllm_mm = None
-    out = {"peak_tflops": FP4_DENSE_NOMINAL_TFLOPS,
-           "peak_source": "nominal dense FP4 (no measured FP4 peak on this pool)",
+    try:
+        peak = measure_fp4_peak(device)
+        peak_tflops = peak["peak_tflops"]
+        peak_source = {"measured": peak, "nominal_tflops": FP4_DENSE_NOMINAL_TFLOPS}
+    except Exception as e:  # the probe needs the whole GPU
+        peak_tflops = FP4_DENSE_NOMINAL_TFLOPS
+        peak_source = f"nominal dense FP4 (tensor-core rate probe failed: {e})"
+    out = {"peak_tflops": peak_tflops, "peak_source": peak_source,
            "method": "per-launch time from one CUDA graph of 20 launches"}
     for k, n in GEMM_SHAPES:
         g = torch.Generator(device=device).manual_seed(k + n)
@@ -601,7 +646,7 @@ def run_gemm_sweep(device, reps: int = 20):
             ms = graph_avg_ms(lambda: cutlass_scaled_fp4_mm(qa, qb, sa, sb, alpha), reps, device)
             res["gemm_us"] = round(ms * 1e3, 2)
             res["gemm_tflops"] = round(flops / (ms * 1e-3) / 1e12, 1)
-            res["gemm_frac"] = round(res["gemm_tflops"] / FP4_DENSE_NOMINAL_TFLOPS, 4)
+            res["gemm_frac"] = round(res["gemm_tflops"] / peak_tflops, 4)
             if vllm_mm is not None:
                 vms = graph_avg_ms(lambda: vllm_mm(qa, qb, sa, sb, alpha, torch.bfloat16), reps,
                                    device)

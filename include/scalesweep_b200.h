@@ -238,6 +238,19 @@ int ssw_nvfp4_gemm_dependent(const uint8_t* a, const uint8_t* b, const uint8_t* 
                              int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
                              int* status, void* stream);
 
+/* Measures the dense FP4 tensor-core rate this GEMM is bounded by.  No
+ * reference counterpart: it gives the measured peak that GEMM roofline
+ * fractions are taken against.  One CTA per SM issues 4 * iters back-to-back
+ * kind::mxf4nvf4 MMAs of 128 x bn x 64 (bn 128 or 256): the GEMM's own
+ * instruction, descriptors and TMEM layout, on operands already in shared
+ * memory, with no loads.  cycles_out (device, one int64 per SM) receives each
+ * CTA's elapsed SM clock cycles, -1 where the bounded completion wait gave up
+ * (then *status is set).  FLOPs per CTA = 2 * 128 * bn * 64 * 4 * iters.
+ * iters <= 16384.  Needs the whole GPU: one CTA holds an SM's TMEM.
+ */
+int ssw_nvfp4_mma_rate_probe(int bn, int iters, long long* cycles_out, int* status,
+                             void* stream);
+
 /*
  * A W4A4 linear layer's activation quantization and GEMM in one call:
  * x [m, k] (bf16/f16) is quantized with the "scalesweep_mse" sweep

@@ -46,6 +46,7 @@ _SIGNATURES = {
                               _c_p, _c_p]),
     "ssw_nvfp4_gemm_dependent": (_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _i64,
                                         _c_p, _i64, _c_p, _c_p]),
+    "ssw_nvfp4_mma_rate_probe": (_int, [_int, _int, _c_p, _c_p, _c_p]),
     "ssw_global_scale_inv_noalloc_max_numel": (_i64, []),
     "ssw_global_scale_inv_noalloc": (_int, [_c_p, _int, _i64, _f32, _c_p, _c_p, _c_p]),
 }

@@ -395,6 +395,23 @@ int ssw_nvfp4_gemm_dependent(const uint8_t* a, const uint8_t* b, const uint8_t* 
                      workspace, workspace_bytes, status, stream, true);
 }
 
+int ssw_nvfp4_mma_rate_probe(int bn, int iters, long long* cycles_out, int* status,
+                             void* stream) {
+  g_last_error.clear();
+  if (bn != 128 && bn != 256)
+    return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_mma_rate_probe: bn must be 128 or 256");
+  if (iters <= 0 || iters > (1 << 14))
+    return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_mma_rate_probe: iters must be in [1, 16384]");
+  if (!cycles_out) return fail(SSW_ERR_INVALID_ARGUMENT, "nvfp4_mma_rate_probe: null pointer");
+  int sms = 0;
+  int st = device_sms(&sms);
+  if (st != SSW_OK) return st;
+  cudaError_t e = ssw::gemm::launch_mma_peak(bn, iters, sms, cycles_out, status,
+                                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "nvfp4_mma_rate_probe launch");
+  return SSW_OK;
+}
+
 int64_t ssw_nvfp4_quant_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   int sms = 0;
   if (m <= 0 || n <= 0 || k <= 0 || n % 64 || k % 256 || device_sms(&sms) != SSW_OK) return 0;

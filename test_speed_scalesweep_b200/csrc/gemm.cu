@@ -1377,6 +1377,67 @@ cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, const char** why
   return cudaGetLastError();
 }
 
+// Dense FP4 tensor-core rate: one CTA per SM issues back-to-back
+// kind::mxf4nvf4 MMAs (128 x BN x 64, the GEMM kernel's own instruction,
+// descriptors and TMEM layout) on tiles already in shared memory, with no
+// loads, scale copies or epilogue.  The operands are whatever the shared
+// memory and TMEM hold: every E2M1 code is a finite value, and the results are
+// never read.  The MMA count per CTA stays small enough that the bounded
+// completion wait cannot give up before the MMAs finish.
+constexpr int kPeakThreads = 128;
+constexpr size_t kPeakSmem = 200 * 1024;  // forces one CTA per SM (TMEM is not shared)
+
+template <int BN>
+__global__ void __launch_bounds__(kPeakThreads, 1)
+    nvfp4_mma_peak_kernel(int iters, long long* cycles, int* status) {
+  using T = Tile<BN, 1>;
+  extern __shared__ __align__(1024) uint8_t peak_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(peak_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __shared__ uint64_t done_bar;
+  __shared__ uint32_t tmem_slot;
+  const int warp = threadIdx.x >> 5;
+  constexpr uint32_t kCols = 512;
+  if (threadIdx.x == 0) {
+    mbar_init(&done_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_slot)),
+                 "r"(kCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = tmem_slot;
+  if (threadIdx.x == 0) {
+    const uint32_t a_base = smem_u32(smem), b_base = smem_u32(smem + kATile);
+    const uint32_t col_sfa = tmem + BN, col_sfb = col_sfa + 16;
+    const long long t0 = clock64();
+    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint64_t adesc = smem_desc(a_base + 32 * j, 16, 1024, kLayoutSW128);
+        const uint64_t bdesc = smem_desc(b_base + 32 * j, 16, 1024, kLayoutSW128);
+        mma_nvf4(tmem, adesc, bdesc, T::kIdesc, col_sfa + 4 * j,
+                 col_sfb + 4 * T::kSFBSlabs * j, (it | j) != 0);
+      }
+    }
+    mma_commit(&done_bar);
+    const bool ok = mbar_wait(&done_bar, 0);
+    const long long t1 = clock64();
+    if (!ok) record_error(status, 1);
+    cycles[blockIdx.x] = ok ? t1 - t0 : -1;
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
+}
+
 }  // namespace
 
 cudaError_t launch(const GemmArgs& g, int splits, cudaStream_t stream, const char** why) {
@@ -1388,6 +1449,25 @@ cudaError_t launch(const GemmArgs& g, int splits, cudaStream_t stream, const cha
   if (tile_n == 256) return launch_bn<256, 4>(g, 1, stream, why);
   if (tile_n == 64) return launch_bn<64, 7>(g, 1, stream, why);
   return launch_bn<128, 3>(g, splits, stream, why);
+}
+
+
+cudaError_t launch_mma_peak(int bn, int iters, int ctas, long long* cycles, int* status,
+                            cudaStream_t stream) {
+  if (bn == 256) {
+    cudaError_t e = cudaFuncSetAttribute(nvfp4_mma_peak_kernel<256>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kPeakSmem);
+    if (e != cudaSuccess) return e;
+    nvfp4_mma_peak_kernel<256><<<ctas, kPeakThreads, kPeakSmem, stream>>>(iters, cycles, status);
+  } else {
+    cudaError_t e = cudaFuncSetAttribute(nvfp4_mma_peak_kernel<128>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kPeakSmem);
+    if (e != cudaSuccess) return e;
+    nvfp4_mma_peak_kernel<128><<<ctas, kPeakThreads, kPeakSmem, stream>>>(iters, cycles, status);
+  }
+  return cudaGetLastError();
 }
 
 }  // namespace gemm

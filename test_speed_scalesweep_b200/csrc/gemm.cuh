@@ -30,6 +30,11 @@ size_t smem_bytes();
 int choose_splits(int64_t m, int64_t n, int64_t k, int device_sms);
 size_t workspace_bytes(int64_t m, int64_t n, int64_t k, int splits);
 cudaError_t launch(const GemmArgs& g, int splits, cudaStream_t stream, const char** why);
+// Dense FP4 tensor-core rate probe: `ctas` CTAs (one per SM) each issue
+// 4 * iters MMAs of 128 x bn x 64 (bn 128 or 256) and write their elapsed
+// SM clock cycles (-1 if the bounded completion wait gave up).
+cudaError_t launch_mma_peak(int bn, int iters, int ctas, long long* cycles, int* status,
+                            cudaStream_t stream);
 
 }  // namespace gemm
 }  // namespace ssw

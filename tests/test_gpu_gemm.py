@@ -157,3 +157,23 @@ def test_dependent_gemm_equals_plain_gemm(lib, m, n, k):
     torch.cuda.synchronize()
     for o in outs:
         assert torch.equal(o, ref)
+
+
+def test_mma_rate_probe_reports_every_sm(lib):
+    """The dense FP4 rate probe (the measured peak GEMM fractions use): every
+    SM's CTA finishes its MMAs within the bounded wait, at a per-cycle rate
+    near the tensor pipe's 32768 FP4 FLOPs per SM cycle."""
+    import ctypes
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    cycles = torch.zeros(sms, dtype=torch.int64, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for bn in (128, 256):
+        st = lib.ssw_nvfp4_mma_rate_probe(bn, 256, ctypes.c_void_p(cycles.data_ptr()),
+                                          ctypes.c_void_p(status.data_ptr()), None)
+        assert st == 0
+        torch.cuda.synchronize()
+        assert status.item() == 0 and int(cycles.min().item()) > 0
+        per_cycle = 2.0 * 128 * bn * 64 * 4 * 256 / float(cycles.median().item())
+        assert 8000 < per_cycle < 70000, per_cycle
+    assert lib.ssw_nvfp4_mma_rate_probe(64, 256, ctypes.c_void_p(cycles.data_ptr()), None,
+                                        None) != 0
