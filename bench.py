@@ -728,10 +728,15 @@ def cpu_sample_rate(rows_hint: int, budget_s: float = 12.0):
     dt = max(time.perf_counter() - t, 1e-4)
     rows = int(min(rows_hint, max(probe_rows, probe_rows * budget_s / dt)))
     rows = max(probe_rows, rows // 64 * 64)
-    x = gi.outlier_activations(rows, K_DIM, seed=4243)
+    # at most 16384 freshly drawn rows, quantized as often as the budget asks
+    chunk = min(rows, 16384)
+    reps = max(1, rows // chunk)
+    rows = reps * chunk
+    x = gi.outlier_activations(chunk, K_DIM, seed=4243)
     gsi = gi.torch_style_gsi(x, FP8_MAX)
     t = time.perf_counter()
-    oracle.quantize(x, gsi, nthreads=threads)
+    for _ in range(reps):
+        oracle.quantize(x, gsi, nthreads=threads)
     dt = time.perf_counter() - t
     # config 1 (128 x 4096) and the config-2 shapes with M <= 1024 at K = 4096:
     # median of 5 runs after one warm-up, ms per call
@@ -750,8 +755,9 @@ def cpu_sample_rate(rows_hint: int, budget_s: float = 12.0):
                               "GB/s": round(m * k * BYTES_PER_ELEM / (ms * 1e-3) / 1e9, 4)}
     return {"value": round(rows * K_DIM * BYTES_PER_ELEM / dt / 1e9, 4), "unit": UNIT,
             "cores": threads, "kind": "port",
-            "sample": f"{rows} x {K_DIM} rows of the workload ({rows * K_DIM // 16} blocks), "
-                      f"{dt:.2f} s, oracle/scalesweep_oracle.c with {threads} OpenMP threads",
+            "sample": f"{rows} x {K_DIM} rows of the workload ({rows * K_DIM // 16} blocks; "
+                      f"{reps} x a {chunk}-row draw), {dt:.2f} s, oracle/scalesweep_oracle.c "
+                      f"with {threads} OpenMP threads",
             "shapes": shapes}
 
 
